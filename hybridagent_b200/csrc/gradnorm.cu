@@ -1,0 +1,159 @@
+// Multi-tensor sum of squared gradients for the global norm (sm_100a).
+//
+// Replaces the per-tensor `grad.float().square().sum()` loop of
+// hybrid_rl/optimizer.py:149-151 (three eager kernels and ~18 bytes of traffic per
+// element) with one read of each gradient (2 bytes per bf16 element).
+//
+// Accuracy and determinism: squares of bf16/fp16 values are exact in fp32; each thread
+// sums one 16-byte vector's squares pairwise in fp32, widens that to fp64 and
+// accumulates in fp64; warps and the CTA combine in fixed trees; every chunk writes its
+// own fp64 partial and one CTA adds the partials in a fixed order.  The result therefore
+// depends only on the data and HA_SUMSQ_CHUNK, not on scheduling, and is far closer to
+// the exact sum than the reference's fp32 accumulation.  NaN and Inf propagate, so a
+// non-finite gradient anywhere makes the sum non-finite (the caller's skip decision).
+#include "ha_common.cuh"
+
+namespace ha {
+namespace {
+
+constexpr int64_t kChunk = HA_SUMSQ_CHUNK;
+
+template <int DT>
+struct Vec;  // elements per 16-byte load
+template <>
+struct Vec<HA_F32> {
+  static constexpr int n = 4;
+};
+template <>
+struct Vec<HA_BF16> {
+  static constexpr int n = 8;
+};
+template <>
+struct Vec<HA_F16> {
+  static constexpr int n = 8;
+};
+
+template <int DT>
+__device__ __forceinline__ float sq(float x) {
+  return __fmul_rn(x, x);  // exact for 16-bit inputs; fp32 inputs round like torch's square()
+}
+
+// Pairwise fp32 sum of the squares of one 16-byte vector.
+template <int DT>
+__device__ __forceinline__ float vec_sumsq(uint4 w) {
+  if constexpr (DT == HA_F32) {
+    const float a = sq<DT>(__uint_as_float(w.x)), b = sq<DT>(__uint_as_float(w.y));
+    const float c = sq<DT>(__uint_as_float(w.z)), d = sq<DT>(__uint_as_float(w.w));
+    return __fadd_rn(__fadd_rn(a, b), __fadd_rn(c, d));
+  } else {
+    float q[8];
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      q[2 * i] = sq<DT>(Elem<DT>::widen(uint16_t(words[i] & 0xffffu)));
+      q[2 * i + 1] = sq<DT>(Elem<DT>::widen(uint16_t(words[i] >> 16)));
+    }
+    return __fadd_rn(__fadd_rn(__fadd_rn(q[0], q[1]), __fadd_rn(q[2], q[3])),
+                     __fadd_rn(__fadd_rn(q[4], q[5]), __fadd_rn(q[6], q[7])));
+  }
+}
+
+__device__ __forceinline__ double block_sum(double x, double* smem) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) smem[warp] = x;
+  __syncthreads();
+  const int nwarps = blockDim.x >> 5;
+  if (warp == 0) {
+    x = lane < nwarps ? smem[lane] : 0.0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  }
+  return x;  // valid in thread 0
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kThreads) sumsq_kernel(const ha_tensor* __restrict__ tensors,
+                                                         const ha_chunk* __restrict__ chunks,
+                                                         double* __restrict__ partials) {
+  __shared__ StagedChunk sc;
+  __shared__ double red[kThreads / 32];
+  stage_chunk(tensors, chunks, &sc);
+  double acc = 0.0;
+  if (sc.t.grad != 0) {
+    constexpr int V = Vec<DT>::n;
+    using raw = typename Elem<DT>::raw;
+    const raw* grad = reinterpret_cast<const raw*>(sc.t.grad);
+    const int64_t begin = int64_t(sc.index) * kChunk;
+    const int64_t end = min(begin + kChunk, sc.t.numel);
+    if ((sc.t.grad & 15) == 0) {
+      constexpr int kPerPass = kThreads * V;       // elements per CTA pass
+      constexpr int kUnroll = 4;                   // loads in flight per thread
+      int64_t e = begin + int64_t(threadIdx.x) * V;
+      for (; e + int64_t(kUnroll - 1) * kPerPass + V <= end; e += int64_t(kUnroll) * kPerPass) {
+        uint4 w[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) w[u] = __ldcs(reinterpret_cast<const uint4*>(grad + e + u * kPerPass));
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) acc += double(vec_sumsq<DT>(w[u]));
+      }
+      for (; e + V <= end; e += kPerPass) acc += double(vec_sumsq<DT>(__ldcs(reinterpret_cast<const uint4*>(grad + e))));
+      if (e < end) {  // ragged tail of the tensor: at most V-1 elements, one thread
+        float s = 0.0f;
+        for (int64_t k = e; k < end; ++k) s = __fadd_rn(s, sq<DT>(Elem<DT>::widen(grad[k])));
+        acc += double(s);
+      }
+    } else {
+      for (int64_t k = begin + threadIdx.x; k < end; k += kThreads) acc += double(sq<DT>(Elem<DT>::widen(grad[k])));
+    }
+  }
+  acc = block_sum(acc, red);
+  if (threadIdx.x == 0) partials[blockIdx.x] = acc;
+}
+
+// One CTA adds the per-chunk partials: thread i takes partials i, i+1024, ... in order
+// (four interleaved accumulators), then a fixed tree.
+constexpr int kFinalThreads = 1024;
+__global__ void __launch_bounds__(kFinalThreads) finalize_kernel(const double* __restrict__ partials, int64_t n,
+                                                                  double* __restrict__ out) {
+  __shared__ double red[kFinalThreads / 32];
+  double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+  int64_t i = threadIdx.x;
+  for (; i + 3 * kFinalThreads < n; i += 4 * kFinalThreads) {
+    a0 += partials[i];
+    a1 += partials[i + kFinalThreads];
+    a2 += partials[i + 2 * kFinalThreads];
+    a3 += partials[i + 3 * kFinalThreads];
+  }
+  for (; i < n; i += kFinalThreads) a0 += partials[i];
+  double x = block_sum((a0 + a1) + (a2 + a3), red);
+  if (threadIdx.x == 0) out[0] = x;
+}
+
+}  // namespace
+}  // namespace ha
+
+extern "C" int ha_grad_sumsq(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,
+                             int64_t chunk_elems, int grad_dtype, double* d_partials, double* d_out, void* stream) {
+  using namespace ha;
+  if (chunk_elems != HA_SUMSQ_CHUNK) return fail(HA_ERR_INVALID, "ha_grad_sumsq: chunk_elems must be %d", HA_SUMSQ_CHUNK);
+  if (!valid_float_dtype(grad_dtype)) return fail(HA_ERR_UNSUPPORTED, "ha_grad_sumsq: grad dtype %d", grad_dtype);
+  if (n_chunks < 0 || n_chunks > 0x7fffffffLL) return fail(HA_ERR_INVALID, "ha_grad_sumsq: n_chunks %lld", (long long)n_chunks);
+  if (d_out == nullptr) return fail(HA_ERR_INVALID, "ha_grad_sumsq: NULL output");
+  if (n_chunks > 0 && (d_tensors == nullptr || d_chunks == nullptr || d_partials == nullptr))
+    return fail(HA_ERR_INVALID, "ha_grad_sumsq: NULL table or partials");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n_chunks > 0) {
+    const dim3 grid(static_cast<unsigned>(n_chunks));
+    switch (grad_dtype) {
+      case HA_F32: sumsq_kernel<HA_F32><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, d_partials); break;
+      case HA_BF16: sumsq_kernel<HA_BF16><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, d_partials); break;
+      default: sumsq_kernel<HA_F16><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, d_partials); break;
+    }
+    const int rc = check_launch("sumsq_kernel");
+    if (rc != HA_OK) return rc;
+  }
+  finalize_kernel<<<1, kFinalThreads, 0, st>>>(d_partials, n_chunks, d_out);
+  return check_launch("sumsq_finalize_kernel");
+}

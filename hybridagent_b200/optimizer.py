@@ -1,0 +1,501 @@
+"""Drop-in B200 replacement for HybridAgent's ``hybrid_rl.optimizer.ZeroOneAdamW``.
+
+Same constructor, methods, public attributes, ownership and results as the reference
+(hybrid_rl/optimizer.py:12-199); the work runs in ``libhybridagent_b200.so``:
+
+=====================  =============================================  ==========================================
+reference              what it does there                             here
+=====================  =============================================  ==========================================
+``__init__`` :13-86    greedy ownership, fp32 master/m/v per owned    same ownership; master/m/v live in one
+                       tensor                                         packed fp32 buffer per dtype class, and at
+                                                                      world > 1 the parameters are re-homed into
+                                                                      an owner-major packed buffer
+``all_reduce_grads``   used-mask MAX all-reduce; per owner, 64 Mi-    used-mask MAX (uint8, NCCL); one multi-tensor
+:95-143                element bf16 buckets packed, ``dist.reduce``,  pack kernel; ONE NCCL reduce-scatter; owned
+                       owner clones                                   grads become views of the reduced segment
+``clip_grad_norm``     per-tensor ``float().square().sum()``, fp32    one multi-tensor sum-of-squares kernel (fp64
+:145-160               all-reduce, ``float(sqrt)``, bf16 ``mul_``     partials, fixed order), one 8-byte NCCL
+                                                                      all-reduce; the clip is folded into ``step``
+``step`` :162-194      ~13 eager kernels per tensor, then one         one fused AdamW kernel per dtype class (28
+                       ``dist.broadcast`` per tensor                  B/param for bf16), ONE NCCL all-gather
+=====================  =============================================  ==========================================
+
+Numerics: every element is updated with the rounding torch's CUDA kernels give the
+reference's op sequence, so master / exp_avg / exp_avg_sq and the parameter copy equal
+the reference run on CUDA bit for bit.  The global norm is summed more accurately than
+the reference's fp32 sum (fp64 partials), so it agrees to about 1e-7 relative; both are
+rounded to fp32 before the square root as the reference does.  A non-finite gradient
+makes the norm non-finite exactly where the reference's does.
+
+Deliberate differences (documented surface):
+
+* ``clip_grad_norm`` records the clip factor and ``step`` applies it while reading each
+  gradient (same arithmetic as the reference's in-place ``grad.mul_``), so between the
+  two calls -- and after ``step`` -- ``p.grad`` holds the unclipped values.  Call
+  :meth:`apply_pending_clip` to scale the gradients in place instead.  A second
+  ``clip_grad_norm`` or an ``all_reduce_grads`` before ``step`` applies it first, so
+  chained calls see exactly the reference's values.
+* At world_size > 1 ``param.data`` of every parameter is re-bound at construction to a
+  view of the packed parameter buffer (values unchanged) so the all-gather writes the
+  model's weights in place; parameters must not be re-bound afterwards.
+* ``use_8bit=True`` (bitsandbytes PagedAdamW8bit, optimizer.py:76-86) is not provided.
+* ``state_dict`` / ``load_state_dict`` are new (the reference has neither).
+"""
+from __future__ import annotations
+
+import ctypes
+from collections.abc import MutableMapping
+
+import numpy as np
+import torch
+
+from . import _lib, layout
+from ._lib import HA_ADAMW_CHUNK, HA_BF16, HA_F16, HA_F32, HA_F64, HA_SUMSQ_CHUNK, HA_U8
+
+_CODES = {torch.float32: HA_F32, torch.bfloat16: HA_BF16, torch.float16: HA_F16}
+_TORCH = {v: k for k, v in _CODES.items()}
+STATE_FORMAT = "hybridagent_b200.zero1_adamw/1"
+
+
+class _Table:
+    """A host table (numpy structured array) mirrored in device memory.
+
+    ``upload()`` copies the current host contents through one of a small ring of pinned
+    buffers, so rewriting the table never waits for the GPU to consume an earlier copy
+    (a ring slot is reused only after its previous copy has completed)."""
+
+    RING = 3
+
+    def __init__(self, n: int, dtype: np.dtype, device: torch.device):
+        self.np = np.zeros(max(n, 1), dtype=dtype)
+        nbytes = self.np.nbytes
+        self.dev = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        self._ring = [torch.empty(nbytes, dtype=torch.uint8, pin_memory=True) for _ in range(self.RING)]
+        self._events: list[torch.cuda.Event | None] = [None] * self.RING
+        self._next = 0
+
+    def upload(self) -> None:
+        k = self._next
+        self._next = (k + 1) % self.RING
+        if self._events[k] is not None:
+            self._events[k].synchronize()
+        buf = self._ring[k]
+        np.copyto(buf.numpy(), self.np.view(np.uint8))
+        self.dev.copy_(buf, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._events[k] = ev
+
+    @property
+    def ptr(self) -> int:
+        return self.dev.data_ptr()
+
+
+class _ParamSteps(MutableMapping):
+    """``param_steps`` of the reference (index -> per-tensor step count) backed by an array."""
+
+    def __init__(self, counts: np.ndarray, owned: list[int]):
+        self._counts = counts
+        self._owned = set(owned)
+        self._order = list(owned)
+
+    def __getitem__(self, i: int) -> int:
+        if i not in self._owned:
+            raise KeyError(i)
+        return int(self._counts[i])
+
+    def __setitem__(self, i: int, v: int) -> None:
+        if i not in self._owned:
+            raise KeyError(f"tensor {i} is not owned by this rank")
+        self._counts[i] = int(v)
+
+    def __delitem__(self, i: int) -> None:
+        raise TypeError("param_steps entries cannot be removed")
+
+    def __iter__(self):
+        return iter(self._order)
+
+    def __len__(self) -> int:
+        return len(self._order)
+
+    def __repr__(self) -> str:
+        return repr(dict(self.items()))
+
+
+class _Class:
+    """Device state of one dtype class on this rank."""
+
+    def __init__(self, opt: "ZeroOneAdamW", cls: layout.DtypeClass):
+        self.code = cls.code
+        self.dtype = _TORCH[cls.code]
+        self.layout = cls
+        self.owned = cls.owned(opt.owner, opt.rank)
+        dev = opt.device
+        W, r = opt.world, opt.rank
+        numel = opt._numels
+        # --- packed parameter / gradient buffers (world > 1)
+        self.packed_param = self.packed_grad = None
+        if W > 1:
+            self.packed_param = torch.empty(W * cls.seg_len, dtype=self.dtype, device=dev)
+            self.packed_grad = torch.zeros(W * cls.seg_len, dtype=self.dtype, device=dev)
+            for i in cls.indices:
+                p = opt.params[i]
+                start = opt.owner[i] * cls.seg_len + cls.offset[i]
+                slot = self.packed_param[start:start + numel[i]].view(p.shape)
+                slot.copy_(p.data)
+                p.data = slot
+        # --- fp32 state of the owned tensors
+        own_len = max(cls.own_len[r], layout.ALIGN)
+        self.exp_avg_buf = torch.zeros(own_len, dtype=torch.float32, device=dev)
+        self.exp_avg_sq_buf = torch.zeros(own_len, dtype=torch.float32, device=dev)
+        self.master_buf = None if self.code == HA_F32 else torch.empty(own_len, dtype=torch.float32, device=dev)
+        for i in self.owned:
+            p = opt.params[i]
+            o = cls.offset[i]
+            opt.exp_avg[i] = self.exp_avg_buf[o:o + numel[i]].view(p.shape)
+            opt.exp_avg_sq[i] = self.exp_avg_sq_buf[o:o + numel[i]].view(p.shape)
+            if self.code == HA_F32:
+                opt.master[i] = p.data  # optimizer.py:71-73: the fp32 parameter is the master
+                opt.master_is_parameter[i] = True
+            else:
+                opt.master[i] = self.master_buf[o:o + numel[i]].view(p.shape)
+                opt.master[i].copy_(p.data)  # float() of the parameter
+                opt.master_is_parameter[i] = False
+        # --- device tables
+        self.table = _Table(len(self.owned), _lib.TENSOR_DTYPE, dev)
+        tab = self.table.np
+        for k, i in enumerate(self.owned):
+            tab[k]["master"] = opt.master[i].data_ptr()
+            tab[k]["exp_avg"] = opt.exp_avg[i].data_ptr()
+            tab[k]["exp_avg_sq"] = opt.exp_avg_sq[i].data_ptr()
+            tab[k]["param"] = 0 if self.code == HA_F32 else opt.params[i].data_ptr()
+            tab[k]["numel"] = numel[i]
+        owned_numels = [numel[i] for i in self.owned]
+        self.lrs = np.ascontiguousarray([opt.lrs[i] for i in self.owned], dtype=np.float64)
+        self.adamw_chunks = self._device_chunks(owned_numels, HA_ADAMW_CHUNK, dev)
+        self.sumsq_chunks = self._device_chunks(owned_numels, HA_SUMSQ_CHUNK, dev)
+        self.partials = torch.empty(max(self.sumsq_chunks[1], 1), dtype=torch.float64, device=dev)
+        # --- pack table (world > 1): every tensor of the class -> its slot in packed_grad
+        self.pack = None
+        if W > 1:
+            self.pack = _Table(len(cls.indices), _lib.COPY_DTYPE, dev)
+            cp = self.pack.np
+            base = self.packed_grad.data_ptr()
+            esz = self.packed_grad.element_size()
+            self.slot_ptr = {}
+            for k, i in enumerate(cls.indices):
+                addr = base + (opt.owner[i] * cls.seg_len + cls.offset[i]) * esz
+                self.slot_ptr[i] = addr
+                cp[k]["dst"] = addr
+                cp[k]["numel"] = numel[i]
+            self.pack_chunks = self._device_chunks([numel[i] for i in cls.indices], HA_ADAMW_CHUNK, dev)
+            # reduced gradient views handed to the caller as p.grad (optimizer.py:141)
+            own0 = r * cls.seg_len
+            self.grad_view = {i: self.packed_grad[own0 + cls.offset[i]:own0 + cls.offset[i] + numel[i]]
+                              .view(opt.params[i].shape) for i in self.owned}
+
+    @staticmethod
+    def _device_chunks(numels: list[int], chunk: int, dev) -> tuple[torch.Tensor | None, int]:
+        tab = layout.chunk_table(numels, chunk)
+        if len(tab) == 0:
+            return None, 0
+        t = torch.from_numpy(tab.view(np.uint8).copy()).to(dev)
+        return t, len(tab)
+
+
+class ZeroOneAdamW:
+    """ZeRO-1 AdamW over CUDA parameters (drop-in for hybrid_rl.optimizer.ZeroOneAdamW)."""
+
+    def __init__(self, param_groups, *, rank: int, world_size: int, betas=(0.9, 0.999), eps: float = 1e-8,
+                 weight_decay: float = 0.0, use_8bit: bool = False):
+        # argument handling and errors as optimizer.py:24-44
+        self.rank = int(rank)
+        self.world = int(world_size)
+        self.betas = tuple(float(value) for value in betas)
+        self.eps = float(eps)
+        self.weight_decay = float(weight_decay)
+        self.use_8bit = bool(use_8bit)
+        if len(self.betas) != 2 or any(not 0.0 <= value < 1.0 for value in self.betas):
+            raise ValueError("betas must contain two values in [0, 1)")
+        if self.world < 1 or not 0 <= self.rank < self.world:
+            raise ValueError(f"invalid rank/world {self.rank}/{self.world}")
+        self.step_count = 0
+        flat: list[tuple[torch.nn.Parameter, float]] = []
+        seen: set[int] = set()
+        for group in param_groups:
+            for parameter in group["params"]:
+                if parameter.requires_grad and id(parameter) not in seen:
+                    seen.add(id(parameter))
+                    flat.append((parameter, float(group["lr"])))
+        if not flat:
+            raise ValueError("ZeroOneAdamW received no trainable parameters")
+        if self.use_8bit:
+            raise NotImplementedError("use_8bit (bitsandbytes PagedAdamW8bit) is not provided by hybridagent_b200")
+        self.params = [p for p, _ in flat]
+        self.lrs = [lr for _, lr in flat]
+        self.device = self.params[0].device
+        if self.device.type != "cuda":
+            raise RuntimeError(f"hybridagent_b200.ZeroOneAdamW runs on CUDA devices only; parameters are on "
+                               f"{self.device} (there is no CPU path)")
+        for p in self.params:
+            if p.device != self.device:
+                raise RuntimeError(f"all parameters must be on one device: {p.device} vs {self.device}")
+            if p.dtype not in _CODES:
+                raise TypeError(f"unsupported parameter dtype {p.dtype}")
+            if not p.is_contiguous():
+                raise ValueError("parameters must be contiguous")
+        _lib.lib()  # fail loudly now if the CUDA library is missing
+        self._numels = [p.numel() for p in self.params]
+        with torch.cuda.device(self.device):
+            self._plan = layout.plan(self._numels, [_CODES[p.dtype] for p in self.params], self.world)
+            self.owner = list(self._plan.owner)
+            self.master: dict[int, torch.Tensor] = {}
+            self.master_is_parameter: dict[int, bool] = {}
+            self.exp_avg: dict[int, torch.Tensor] = {}
+            self.exp_avg_sq: dict[int, torch.Tensor] = {}
+            self._steps = np.zeros(len(self.params), dtype=np.int64)
+            owned_all = [i for i in range(len(self.params)) if self.owner[i] == self.rank]
+            self.param_steps = _ParamSteps(self._steps, owned_all)
+            self.owned_numel = sum(self._numels[i] for i in owned_all)
+            self._comm = None
+            if self.world > 1:
+                from .comm import NcclComm
+                self._comm = NcclComm(self.rank, self.world)
+            self._classes = [_Class(self, c) for c in self._plan.classes]
+            self._norm_buf = torch.zeros(len(self._classes), dtype=torch.float64, device=self.device)
+            self._used_dev = torch.zeros(len(self.params), dtype=torch.uint8, device=self.device)
+            torch.cuda.current_stream().synchronize()
+        self._pending_clip: float | None = None
+        self.timer = None  # optional phase timer: .begin(name) / .end(name) around device work
+
+    # ---------------------------------------------------------------- helpers
+    def _phase(self, name: str, start: bool) -> None:
+        if self.timer is not None:
+            (self.timer.begin if start else self.timer.end)(name)
+
+    @staticmethod
+    def _stream() -> int:
+        return torch.cuda.current_stream().cuda_stream
+
+    def _owned_grads(self, c: _Class) -> tuple[list[torch.Tensor | None], np.ndarray]:
+        grads, ptrs = [], np.zeros(len(c.owned), dtype=np.uint64)
+        for k, i in enumerate(c.owned):
+            g = self.params[i].grad
+            if g is not None:
+                if g.dtype != c.dtype or g.numel() != self._numels[i] or g.device != self.device:
+                    raise RuntimeError(f"gradient of tensor {i} has dtype {g.dtype}, {g.numel()} elements on "
+                                       f"{g.device}; expected {c.dtype}, {self._numels[i]}, {self.device}")
+                if not g.is_contiguous():
+                    g = g.contiguous()
+                ptrs[k] = g.data_ptr()
+            grads.append(g)
+        return grads, ptrs
+
+    def _upload_table(self, c: _Class, grad_ptrs: np.ndarray, advance: bool) -> None:
+        tab = c.table.np[:len(c.owned)]
+        tab["grad"] = grad_ptrs
+        if c.code != HA_F32 and self.world == 1:
+            tab["param"] = np.fromiter((self.params[i].data.data_ptr() for i in c.owned), dtype=np.uint64,
+                                       count=len(c.owned))
+        if advance:
+            idx = np.asarray(c.owned, dtype=np.int64)
+            used = grad_ptrs != 0
+            self._steps[idx[used]] += 1  # optimizer.py:181, only tensors that have a gradient
+            steps = np.ascontiguousarray(self._steps[idx])
+            _lib.call("ha_fill_step_scalars", len(c.owned), _lib.np_ptr(c.lrs), _lib.np_ptr(steps),
+                      self.betas[0], self.betas[1], self.weight_decay, _lib.np_ptr(tab))
+        c.table.upload()
+
+    # ---------------------------------------------------------------- reference surface
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        """optimizer.py:88-93."""
+        self._pending_clip = None
+        for parameter in self.params:
+            if set_to_none:
+                parameter.grad = None
+            elif parameter.grad is not None:
+                parameter.grad.zero_()
+
+    @torch.no_grad()
+    def all_reduce_grads(self) -> None:
+        """Sum every rank's gradient onto its owner (optimizer.py:95-143).  Tensors with no
+        gradient on any rank keep grad=None; owners receive views of the reduced segment
+        and every other rank None.  All ranks must call it."""
+        if self.world == 1:
+            return
+        self.apply_pending_clip()
+        with torch.cuda.device(self.device):
+            local = np.fromiter((p.grad is not None for p in self.params), dtype=np.uint8, count=len(self.params))
+            self._used_dev.copy_(torch.from_numpy(local), non_blocking=False)
+            self._comm.all_reduce_max(self._used_dev, HA_U8)
+            used = self._used_dev.cpu().numpy().astype(bool)
+            keep = []  # gradients that must stay alive until the pack kernel has read them
+            for c in self._classes:
+                cp = c.pack.np
+                for k, i in enumerate(c.layout.indices):
+                    p = self.params[i]
+                    if p.data.data_ptr() != c.packed_param.data_ptr() + (
+                            self.owner[i] * c.layout.seg_len + c.layout.offset[i]) * p.element_size():
+                        raise RuntimeError(f"parameter {i} was re-bound after the optimizer was built")
+                    g = p.grad
+                    if g is None or not used[i]:
+                        cp[k]["src"] = 0
+                        continue
+                    if g.dtype != c.dtype or g.numel() != self._numels[i]:
+                        raise RuntimeError(f"gradient of tensor {i}: {g.dtype} x {g.numel()}")
+                    if not g.is_contiguous():
+                        g = g.contiguous()
+                    keep.append(g)
+                    cp[k]["src"] = g.data_ptr()  # equal to dst when the gradient already lives in its slot
+                c.pack.upload()
+                self._phase("pack", True)
+                if c.pack_chunks[1]:
+                    _lib.call("ha_gather", c.pack.ptr, c.pack_chunks[0].data_ptr(), c.pack_chunks[1], HA_ADAMW_CHUNK,
+                              c.packed_grad.element_size(), self._stream())
+                self._phase("pack", False)
+                self._phase("reduce_scatter", True)
+                own = c.packed_grad.data_ptr() + self.rank * c.layout.seg_len * c.packed_grad.element_size()
+                self._comm.reduce_scatter(c.packed_grad.data_ptr(), own, c.layout.seg_len, c.code)
+                self._phase("reduce_scatter", False)
+            del keep
+            for c in self._classes:
+                for i in c.layout.indices:
+                    if used[i] and self.owner[i] == self.rank:
+                        self.params[i].grad = c.grad_view[i]
+                    else:
+                        self.params[i].grad = None
+
+    @torch.no_grad()
+    def clip_grad_norm(self, max_norm: float) -> float:
+        """Global L2 norm of the owned gradients (all ranks), clipping to max_norm
+        (optimizer.py:145-160).  Returns the pre-clip norm."""
+        self.apply_pending_clip()
+        with torch.cuda.device(self.device):
+            self._phase("sumsq", True)
+            for k, c in enumerate(self._classes):
+                _, ptrs = self._owned_grads(c)
+                self._upload_table(c, ptrs, advance=False)
+                chunks, n = c.sumsq_chunks
+                _lib.call("ha_grad_sumsq", c.table.ptr, None if chunks is None else chunks.data_ptr(), n,
+                          HA_SUMSQ_CHUNK, c.code, c.partials.data_ptr(), self._norm_buf[k:].data_ptr(),
+                          self._stream())
+            self._phase("sumsq", False)
+            if self.world > 1:
+                self._comm.all_reduce_sum(self._norm_buf, HA_F64)
+            partial = self._norm_buf.cpu().tolist()
+        total = np.float32(sum(partial))  # the reference's total is an fp32 tensor
+        norm = float(np.sqrt(total))      # float(total.sqrt()), optimizer.py:154
+        if max_norm > 0 and norm > max_norm:
+            self._pending_clip = float(max_norm) / (norm + 1e-6)  # optimizer.py:156
+        return norm
+
+    @torch.no_grad()
+    def apply_pending_clip(self) -> None:
+        """Scales the owned gradients in place by the factor the last clip_grad_norm chose
+        (the reference's ``grad.mul_(scale)``, optimizer.py:157-159); no-op if none."""
+        if self._pending_clip is None:
+            return
+        scale, self._pending_clip = self._pending_clip, None
+        with torch.cuda.device(self.device):
+            for c in self._classes:
+                _, ptrs = self._owned_grads(c)
+                self._upload_table(c, ptrs, advance=False)
+                sc = _lib.AdamwScalars()
+                _lib.call("ha_make_scalars", self.betas[0], self.betas[1], self.eps, self.weight_decay, c.code, 1,
+                          scale, ctypes.byref(sc))
+                chunks, n = c.adamw_chunks
+                if n:
+                    _lib.call("ha_scale_grads", c.table.ptr, chunks.data_ptr(), n, HA_ADAMW_CHUNK, c.code,
+                              sc.clip_mult, self._stream())
+
+    @torch.no_grad()
+    def step(self) -> None:
+        """Fused AdamW over the owned tensors with a gradient, then the parameter
+        all-gather (optimizer.py:162-194)."""
+        self.step_count += 1
+        scale, self._pending_clip = self._pending_clip, None
+        with torch.cuda.device(self.device):
+            self._phase("adamw", True)
+            for c in self._classes:
+                _, ptrs = self._owned_grads(c)
+                self._upload_table(c, ptrs, advance=True)
+                sc = _lib.AdamwScalars()
+                _lib.call("ha_make_scalars", self.betas[0], self.betas[1], self.eps, self.weight_decay, c.code,
+                          0 if scale is None else 1, 0.0 if scale is None else scale, ctypes.byref(sc))
+                chunks, n = c.adamw_chunks
+                if n:
+                    _lib.call("ha_adamw_step", c.table.ptr, chunks.data_ptr(), n, HA_ADAMW_CHUNK, c.code, c.code,
+                              ctypes.byref(sc), self._stream())
+            self._phase("adamw", False)
+            if self.world > 1:
+                self._phase("all_gather", True)
+                for c in self._classes:
+                    own = c.packed_param.data_ptr() + self.rank * c.layout.seg_len * c.packed_param.element_size()
+                    self._comm.all_gather(own, c.packed_param.data_ptr(), c.layout.seg_len, c.code)
+                self._phase("all_gather", False)
+
+    def state_summary(self) -> str:
+        """optimizer.py:196-199."""
+        return (f"ZeRO-1 FP32 AdamW: {len(self.params)} tensors; rank {self.rank} owns "
+                f"{self.owned_numel / 1e6:.1f}M parameters")
+
+    # ---------------------------------------------------------------- checkpointing (new surface)
+    def state_dict(self) -> dict:
+        """This rank's shard: fp32 master / exp_avg / exp_avg_sq and the step counts of its
+        owned tensors (CPU copies), keyed by flat parameter index, plus what identifies the
+        layout.  Loading it into an optimizer built over the same parameters, rank and
+        world size resumes bit-identically."""
+        torch.cuda.current_stream(self.device).synchronize()
+        owned = list(self.param_steps)
+        return {
+            "format": STATE_FORMAT,
+            "world": self.world,
+            "rank": self.rank,
+            "step_count": self.step_count,
+            "owner": list(self.owner),
+            "numels": list(self._numels),
+            "lrs": list(self.lrs),
+            "betas": self.betas,
+            "eps": self.eps,
+            "weight_decay": self.weight_decay,
+            "param_steps": {i: int(self._steps[i]) for i in owned},
+            "master": {i: self.master[i].detach().to("cpu", copy=True) for i in owned},
+            "exp_avg": {i: self.exp_avg[i].detach().to("cpu", copy=True) for i in owned},
+            "exp_avg_sq": {i: self.exp_avg_sq[i].detach().to("cpu", copy=True) for i in owned},
+        }
+
+    @torch.no_grad()
+    def load_state_dict(self, state: dict) -> None:
+        if state.get("format") != STATE_FORMAT:
+            raise ValueError(f"not a {STATE_FORMAT} state dict")
+        for key, mine in (("world", self.world), ("rank", self.rank), ("owner", list(self.owner)),
+                          ("numels", list(self._numels))):
+            if state[key] != mine:
+                raise ValueError(f"state dict {key} does not match this optimizer")
+        owned = list(self.param_steps)
+        if sorted(state["param_steps"]) != sorted(owned):
+            raise ValueError("state dict holds a different set of owned tensors")
+        for i in owned:
+            for name, dst in (("master", self.master[i]), ("exp_avg", self.exp_avg[i]),
+                              ("exp_avg_sq", self.exp_avg_sq[i])):
+                src = state[name][i]
+                if src.shape != dst.shape:
+                    raise ValueError(f"{name}[{i}] has shape {tuple(src.shape)}, expected {tuple(dst.shape)}")
+                dst.copy_(src.to(dst.device, torch.float32))
+            self._steps[i] = int(state["param_steps"][i])
+        self.step_count = int(state["step_count"])
+        self._pending_clip = None
+        torch.cuda.current_stream(self.device).synchronize()
+
+    def close(self) -> None:
+        """Releases the NCCL communicator (world_size > 1)."""
+        if self._comm is not None:
+            self._comm.close()
+            self._comm = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+

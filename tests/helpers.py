@@ -1,0 +1,81 @@
+"""Shared test helpers: golden fixtures, oracle replays and the parity criteria."""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+
+from cases import BF16, CASES_BY_NAME, F16, F32, Case
+from oracle import zero1 as Z
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def golden(name: str) -> dict:
+    with np.load(os.path.join(GOLDEN, f"{name}.npz")) as f:
+        return {k: f[k] for k in f.files}
+
+
+def oracle_for(case: Case, form: int) -> Z.OracleZeroOne:
+    """The oracle set up exactly as make_golden.py sets up the reference."""
+    ora = Z.OracleZeroOne(case.initial_params(), [case.dtype] * len(case.shapes), [case.lr] * len(case.shapes),
+                          world=case.world, betas=case.betas, eps=case.eps, weight_decay=case.weight_decay,
+                          form=form)
+    if case.preload_state:
+        for i in range(len(case.shapes)):
+            master, m, v, step = case.preload(i)
+            M, EA, EAS, _ = ora.tensor_state(i)
+            M[:] = master
+            EA[:] = m
+            EAS[:] = v
+            ora.state[ora.owner[i]].param_steps[i] = step
+            ora.params[i] = M if case.dtype == F32 else Z.narrow(master, case.dtype, form)
+    return ora
+
+
+def oracle_replay(case: Case, form: int, norms: list[float] | None = None) -> tuple[Z.OracleZeroOne, list[float]]:
+    """Runs every step of a case; ``norms`` replays externally computed norms (so the clip
+    factor matches the run being compared against)."""
+    ora = oracle_for(case, form)
+    out = []
+    for s in range(case.steps):
+        ora.reduce_grads([case.grads(s, r) for r in range(case.world)])
+        n = ora.clip_grad_norm(case.max_norm, norm=None if norms is None else norms[s])
+        out.append(n)
+        if np.isfinite(n) or case.call_step_after_nonfinite:
+            ora.step()
+    return ora, out
+
+
+def assert_bits_equal(a: np.ndarray, b: np.ndarray, what: str) -> None:
+    a = np.ascontiguousarray(a).reshape(-1)
+    b = np.ascontiguousarray(b).reshape(-1)
+    if a.dtype == np.float32:
+        nan = np.isnan(a) & np.isnan(b)
+        diff = (a.view(np.uint32) != b.view(np.uint32)) & ~nan
+    else:
+        diff = a != b
+        if a.dtype == np.uint16:  # bf16 / fp16 NaN encodings may differ between devices
+            nan = ((a & 0x7FFF) > 0x7F80) & ((b & 0x7FFF) > 0x7F80)
+            diff &= ~nan
+    n = int(diff.sum())
+    assert n == 0, f"{what}: {n} of {a.size} elements differ (first at {int(np.argmax(diff))})"
+
+
+def assert_state_close(a: np.ndarray, b: np.ndarray, what: str, *, max_ulp: int = 2, rel: float = 1e-6) -> None:
+    """fp32 parity criterion: every element within ``max_ulp`` units in the last place, or
+    within ``rel`` of the tensor's RMS magnitude (values crossing or sitting near zero,
+    where one ulp is far below the data's resolution); NaN matches NaN."""
+    a = np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+    b = np.ascontiguousarray(b, dtype=np.float32).reshape(-1)
+    ulp = Z.ulp_distance(a, b)
+    fin = np.isfinite(a) & np.isfinite(b)
+    scale = float(np.sqrt(np.mean(b[fin].astype(np.float64) ** 2))) if fin.any() else 0.0
+    ok = (ulp <= max_ulp) | (fin & (np.abs(a.astype(np.float64) - b) <= rel * scale))
+    bad = ~ok
+    assert not bad.any(), (f"{what}: {int(bad.sum())} of {a.size} elements outside {max_ulp} ulp / rel {rel} "
+                           f"(worst ulp {int(ulp[bad].max())} at {int(np.argmax(bad))})")
+
+
+__all__ = ["BF16", "CASES_BY_NAME", "F16", "F32", "Case", "Z", "golden", "oracle_for", "oracle_replay",
+           "assert_bits_equal", "assert_state_close"]
