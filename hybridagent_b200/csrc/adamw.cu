@@ -33,8 +33,9 @@ struct Scalars {
 //   master.mul_(1 - lr*wd)                          -> master * decay
 //   mean.mul_(b1).add_(g, alpha=1-b1)               -> fma(a1, g, m*b1)
 //   variance.mul_(b2).addcmul_(g, g, value=1-b2)    -> fma(a2, g*g, v*b2)
-//   (variance / c2).sqrt().add_(eps)                -> sqrt(v * (1/c2)) + eps   (CPU-scalar divisor)
-//   master.addcdiv_(mean / c1, denom, value=-lr)    -> fma(-lr, (m * (1/c1)) / denom, master)
+//   (variance / c2).sqrt().add_(eps)                -> sqrt(v * rc2) + eps, rc2 = (float)(1.0 / c2)
+//   master.addcdiv_(mean / c1, denom, value=-lr)    -> fma(-lr, (m * rc1) / denom, master)
+// (torch divides by a Python float by multiplying with its double reciprocal rounded to fp32)
 __device__ __forceinline__ void adamw_elem(const Scalars& s, float decay, float neg_lr, float rc1, float rc2,
                                            float g, float& ms, float& m, float& v) {
   if (s.use_decay) ms = __fmul_rn(ms, decay);

@@ -15,7 +15,7 @@ template <int BYTES>
 __global__ void __launch_bounds__(kThreads) gather_kernel(const ha_copy* __restrict__ copies,
                                                           const ha_chunk* __restrict__ chunks, int64_t chunk_elems) {
   using T = typename std::conditional<BYTES == 2, uint16_t, uint32_t>::type;
-  __shared__ ha_copy c;
+  __shared__ __align__(16) ha_copy c;  // written with 16-byte shared stores
   __shared__ uint32_t index;
   if (threadIdx.x < 2) {
     const ha_chunk ch = chunks[blockIdx.x];

@@ -93,7 +93,7 @@ __device__ __forceinline__ void store4_narrow(void* base, int64_t e, float4 x) {
 
 // The 64-byte tensor descriptor and the chunk index of this CTA, staged in shared memory
 // by four threads (one 16-byte load each).
-struct StagedChunk {
+struct __align__(16) StagedChunk {  // written with 16-byte shared stores
   ha_tensor t;
   uint32_t index;
 };

@@ -115,10 +115,10 @@ extern "C" int ha_fill_step_scalars(int64_t n, const double* lrs, const int64_t*
     const double c2 = 1.0 - std::pow(beta2, static_cast<double>(steps[i]));
     table[i].decay = static_cast<float>(1.0 - lr * weight_decay);  // optimizer.py:185
     table[i].neg_lr = static_cast<float>(-lr);                     // optimizer.py:189 value=-lr
-    // torch's CUDA division by a CPU scalar multiplies by the fp32 reciprocal of the
-    // fp32-rounded divisor, computed on the host in fp32
-    table[i].rc1 = 1.0f / static_cast<float>(c1);
-    table[i].rc2 = 1.0f / static_cast<float>(c2);
+    // torch's CUDA `tensor / python_float` multiplies by the divisor's reciprocal taken
+    // in double and rounded to fp32 once (measured on B200 for every step count)
+    table[i].rc1 = static_cast<float>(1.0 / c1);
+    table[i].rc2 = static_cast<float>(1.0 / c2);
   }
   return HA_OK;
 }

@@ -266,7 +266,8 @@ class ZeroOneAdamW:
             self._used_dev = torch.zeros(len(self.params), dtype=torch.uint8, device=self.device)
             torch.cuda.current_stream().synchronize()
         self._pending_clip: float | None = None
-        self.timer = None  # optional phase timer: .begin(name) / .end(name) around device work
+        self.timer = None  # optional phase timer: .begin(name) / .end(name) around kernel launches
+        self.launches = 0  # kernels of libhybridagent_b200 launched so far
 
     # ---------------------------------------------------------------- helpers
     def _phase(self, name: str, start: bool) -> None:
@@ -352,6 +353,7 @@ class ZeroOneAdamW:
                 if c.pack_chunks[1]:
                     _lib.call("ha_gather", c.pack.ptr, c.pack_chunks[0].data_ptr(), c.pack_chunks[1], HA_ADAMW_CHUNK,
                               c.packed_grad.element_size(), self._stream())
+                    self.launches += 1
                 self._phase("pack", False)
                 self._phase("reduce_scatter", True)
                 own = c.packed_grad.data_ptr() + self.rank * c.layout.seg_len * c.packed_grad.element_size()
@@ -371,14 +373,18 @@ class ZeroOneAdamW:
         (optimizer.py:145-160).  Returns the pre-clip norm."""
         self.apply_pending_clip()
         with torch.cuda.device(self.device):
+            keep = []  # contiguous copies of strided gradients must outlive the launches
+            for c in self._classes:
+                grads, ptrs = self._owned_grads(c)
+                keep.append(grads)
+                self._upload_table(c, ptrs, advance=False)
             self._phase("sumsq", True)
             for k, c in enumerate(self._classes):
-                _, ptrs = self._owned_grads(c)
-                self._upload_table(c, ptrs, advance=False)
                 chunks, n = c.sumsq_chunks
                 _lib.call("ha_grad_sumsq", c.table.ptr, None if chunks is None else chunks.data_ptr(), n,
                           HA_SUMSQ_CHUNK, c.code, c.partials.data_ptr(), self._norm_buf[k:].data_ptr(),
                           self._stream())
+                self.launches += 2 if n else 1
             self._phase("sumsq", False)
             if self.world > 1:
                 self._comm.all_reduce_sum(self._norm_buf, HA_F64)
@@ -397,8 +403,10 @@ class ZeroOneAdamW:
             return
         scale, self._pending_clip = self._pending_clip, None
         with torch.cuda.device(self.device):
+            keep = []
             for c in self._classes:
-                _, ptrs = self._owned_grads(c)
+                grads, ptrs = self._owned_grads(c)
+                keep.append(grads)
                 self._upload_table(c, ptrs, advance=False)
                 sc = _lib.AdamwScalars()
                 _lib.call("ha_make_scalars", self.betas[0], self.betas[1], self.eps, self.weight_decay, c.code, 1,
@@ -407,6 +415,7 @@ class ZeroOneAdamW:
                 if n:
                     _lib.call("ha_scale_grads", c.table.ptr, chunks.data_ptr(), n, HA_ADAMW_CHUNK, c.code,
                               sc.clip_mult, self._stream())
+                    self.launches += 1
 
     @torch.no_grad()
     def step(self) -> None:
@@ -415,17 +424,22 @@ class ZeroOneAdamW:
         self.step_count += 1
         scale, self._pending_clip = self._pending_clip, None
         with torch.cuda.device(self.device):
-            self._phase("adamw", True)
+            launches, keep = [], []
             for c in self._classes:
-                _, ptrs = self._owned_grads(c)
+                grads, ptrs = self._owned_grads(c)
+                keep.append(grads)
                 self._upload_table(c, ptrs, advance=True)
                 sc = _lib.AdamwScalars()
                 _lib.call("ha_make_scalars", self.betas[0], self.betas[1], self.eps, self.weight_decay, c.code,
                           0 if scale is None else 1, 0.0 if scale is None else scale, ctypes.byref(sc))
+                launches.append((c, sc))
+            self._phase("adamw", True)
+            for c, sc in launches:
                 chunks, n = c.adamw_chunks
                 if n:
                     _lib.call("ha_adamw_step", c.table.ptr, chunks.data_ptr(), n, HA_ADAMW_CHUNK, c.code, c.code,
                               ctypes.byref(sc), self._stream())
+                    self.launches += 1
             self._phase("adamw", False)
             if self.world > 1:
                 self._phase("all_gather", True)

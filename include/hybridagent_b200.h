@@ -65,8 +65,8 @@ typedef struct ha_tensor {
   int64_t numel;
   float decay;         /* (float)(1 - lr*weight_decay)          optimizer.py:185 */
   float neg_lr;        /* (float)(-lr)                          optimizer.py:189 */
-  float rc1;           /* 1.0f / (float)(1 - beta1**step)       optimizer.py:182,189 */
-  float rc2;           /* 1.0f / (float)(1 - beta2**step)       optimizer.py:183,188 */
+  float rc1;           /* (float)(1.0 / (1 - beta1**step))      optimizer.py:182,189 */
+  float rc2;           /* (float)(1.0 / (1 - beta2**step))      optimizer.py:183,188 */
 } ha_tensor;
 
 /* One chunk: elements [index*chunk, min((index+1)*chunk, numel)) of table entry `tensor`. */

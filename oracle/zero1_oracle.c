@@ -18,7 +18,8 @@
  *                     neither:           v*b2 + round(round(value*g)*g)
  *   optimizer.py:188  (variance / correction2).sqrt().add_(eps)
  *   optimizer.py:189  mean / correction1
- *                     ORA_DIV_RECIP: x * (1.0f / (float)c)    else  x / (float)c
+ *                     ORA_DIV_RECIP: x * (float)(1.0 / c), the reciprocal taken in
+ *                     double and rounded once     else  x / (float)c
  *   optimizer.py:189  master.addcdiv_(mhat, denom, value=-lr)
  *                     ORA_ADDCDIV_FMA:  fma(value, mhat/denom, master)
  *                     else:             master + round(round(value*mhat)/denom)
@@ -139,7 +140,7 @@ typedef struct {
   float b1, a1;  /* (float)beta1, (float)(1 - beta1) */
   float b2, a2;  /* (float)beta2, (float)(1 - beta2) */
   float c1, c2;  /* (float)correction */
-  float rc1, rc2;/* 1.0f / (float)correction */
+  float rc1, rc2;/* (float)(1.0 / correction) */
   float eps;     /* (float)eps */
   float neg_lr;  /* (float)(-lr) */
   int use_decay; /* `if self.weight_decay:` */
@@ -157,8 +158,8 @@ static ora_consts make_consts(double lr, double beta1, double beta2, double eps,
   k.a2 = (float)(1.0 - beta2);
   k.c1 = (float)c1;
   k.c2 = (float)c2;
-  k.rc1 = 1.0f / k.c1;
-  k.rc2 = 1.0f / k.c2;
+  k.rc1 = (float)(1.0 / c1);
+  k.rc2 = (float)(1.0 / c2);
   k.eps = (float)eps;
   k.neg_lr = (float)(-lr);
   return k;

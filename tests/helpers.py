@@ -77,5 +77,26 @@ def assert_state_close(a: np.ndarray, b: np.ndarray, what: str, *, max_ulp: int 
                            f"(worst ulp {int(ulp[bad].max())} at {int(np.argmax(bad))})")
 
 
-__all__ = ["BF16", "CASES_BY_NAME", "F16", "F32", "Case", "Z", "golden", "oracle_for", "oracle_replay",
-           "assert_bits_equal", "assert_state_close"]
+# ---------------------------------------------------------------- torch conversions
+def torch_dtype(code: int):
+    import torch
+    return {F32: torch.float32, BF16: torch.bfloat16, F16: torch.float16}[code]
+
+
+def to_torch(a: np.ndarray, code: int, shape=None, device="cpu"):
+    """numpy fp32 values / 16-bit patterns -> torch tensor of dtype ``code``."""
+    import torch
+    a = np.ascontiguousarray(a)
+    t = torch.from_numpy(a.copy()) if code == F32 else torch.from_numpy(a.view(np.int16).copy()).view(torch_dtype(code))
+    if shape is not None:
+        t = t.reshape(shape)
+    return t.to(device)
+
+
+def to_numpy(t, code: int) -> np.ndarray:
+    """torch tensor -> numpy fp32 values / 16-bit patterns (flat)."""
+    import torch
+    t = t.detach().to("cpu").contiguous().reshape(-1)
+    if code == F32:
+        return t.numpy().copy()
+    return t.view(torch.int16).numpy().view(np.uint16).copy()

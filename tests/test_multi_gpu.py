@@ -1,0 +1,60 @@
+"""The optimizer at world size 2 on two GPUs over NCCL (skipped with fewer GPUs).
+
+Each rank runs tests/world_worker.py under torchrun on a world-size-2 golden case.  At
+world size 2 the reduce-scatter's sums have one rounding whatever the algorithm, so the
+owners' reduced gradients, norms and states can be held bit for bit to the oracle (torch-
+CUDA form, replaying this run's norms) and to the reference's own gloo run within the
+parity criterion.  The parameters must agree bit for bit across ranks.
+"""
+import os
+import pickle
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from cases import CASES_BY_NAME
+from helpers import Z, assert_bits_equal, assert_state_close, golden, oracle_replay
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _gpus() -> int:
+    import torch
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("name", ["bf16_world2", "fp32_world2"])
+def test_world2_nccl_matches_oracle_and_reference(name, tmp_path):
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29731",
+           os.path.join(HERE, "world_worker.py"), name, str(tmp_path)]
+    proc = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    res = [pickle.load(open(tmp_path / f"rank{r}.pkl", "rb")) for r in range(2)]
+    case = CASES_BY_NAME[name]
+    g = golden(name)
+    assert res[0]["norms"] == res[1]["norms"]
+    assert res[0]["owner"] == g["owner"].tolist()
+    for s, (mine, ref) in enumerate(zip(res[0]["norms"], g["norms"].tolist())):
+        assert Z.isclose_norm(mine, ref, 1e-6), (s, mine, ref)
+    ora, _ = oracle_replay(case, Z.FORM_TORCH_CUDA, norms=res[0]["norms"])
+    for i in range(len(case.shapes)):
+        assert np.array_equal(res[0]["params"][i].view(np.uint8), res[1]["params"][i].view(np.uint8)), i
+        assert_bits_equal(res[0]["params"][i], ora.params[i], f"param[{i}]")
+        owner = res[0]["owner"][i]
+        master, m, v, steps = res[owner]["state"][i]
+        om, oea, oeas, osteps = ora.tensor_state(i)
+        assert steps == osteps == int(g[f"param_steps_{i}"])
+        assert_bits_equal(master, om, f"master[{i}]")
+        assert_bits_equal(m, oea, f"exp_avg[{i}]")
+        assert_bits_equal(v, oeas, f"exp_avg_sq[{i}]")
+        assert_state_close(master, g[f"master_{i}"], f"ref master[{i}]")
+        # after all_reduce_grads only the owner holds a gradient
+        other = 1 - owner
+        assert res[other]["grads"][-1][i] is None

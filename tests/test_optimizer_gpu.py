@@ -1,0 +1,184 @@
+"""The drop-in ZeroOneAdamW at world size 1 on a B200, driven exactly like the
+reference's trainer (zero_grad -> grads -> all_reduce_grads -> clip_grad_norm -> step,
+hybrid_rl/train.py:248-295) over every single-rank golden case.
+
+* state and parameters: bit for bit equal to the oracle's torch-CUDA form replayed with
+  this optimizer's norms, and within the parity criterion of the reference's own CPU
+  results (the golden vectors);
+* norms: within 1e-6 relative of the reference's;
+* skip decisions: the same steps return non-finite norms.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from cases import CASES
+from helpers import Z, assert_bits_equal, assert_state_close, golden, oracle_replay, to_numpy, to_torch
+
+pytestmark = pytest.mark.gpu
+
+NORM_REL = 1e-6
+
+
+def build(case, **kw):
+    import torch
+    from hybridagent_b200 import ZeroOneAdamW
+    params = [torch.nn.Parameter(to_torch(p, case.dtype, s, "cuda")) for p, s in zip(case.initial_params(), case.shapes)]
+    opt = ZeroOneAdamW([{"params": params, "lr": case.lr}], rank=0, world_size=1, betas=case.betas, eps=case.eps,
+                       weight_decay=case.weight_decay, **kw)
+    if case.preload_state:
+        for i, s in enumerate(case.shapes):
+            master, m, v, step = case.preload(i)
+            opt.master[i].copy_(torch.from_numpy(master).reshape(s))
+            opt.exp_avg[i].copy_(torch.from_numpy(m).reshape(s))
+            opt.exp_avg_sq[i].copy_(torch.from_numpy(v).reshape(s))
+            opt.param_steps[i] = step
+            if not opt.master_is_parameter[i]:
+                params[i].data.copy_(opt.master[i].to(params[i].dtype))
+    return params, opt
+
+
+def run_steps(case, params, opt, steps):
+    norms = []
+    for s in steps:
+        opt.zero_grad(set_to_none=True)
+        for p, g, shape in zip(params, case.grads(s, 0), case.shapes):
+            p.grad = None if g is None else to_torch(g, case.dtype, shape, "cuda")
+        opt.all_reduce_grads()
+        n = opt.clip_grad_norm(case.max_norm)
+        norms.append(n)
+        if math.isfinite(n) or case.call_step_after_nonfinite:
+            opt.step()
+    return norms
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c.world == 1], ids=lambda c: c.name)
+def test_matches_oracle_and_reference(case):
+    g = golden(case.name)
+    params, opt = build(case)
+    assert opt.owner == g["owner"].tolist()
+    norms = run_steps(case, params, opt, range(case.steps))
+    for s, (mine, ref) in enumerate(zip(norms, g["norms"].tolist())):
+        assert Z.isclose_norm(mine, ref, NORM_REL), f"step {s}: {mine} vs reference {ref}"
+    ora, _ = oracle_replay(case, Z.FORM_TORCH_CUDA, norms=norms)
+    for i in range(len(case.shapes)):
+        master, m, v, steps = ora.tensor_state(i)
+        assert opt.param_steps[i] == steps == int(g[f"param_steps_{i}"])
+        assert_bits_equal(to_numpy(opt.master[i], 0), master, f"master[{i}]")
+        assert_bits_equal(to_numpy(opt.exp_avg[i], 0), m, f"exp_avg[{i}]")
+        assert_bits_equal(to_numpy(opt.exp_avg_sq[i], 0), v, f"exp_avg_sq[{i}]")
+        assert_bits_equal(to_numpy(params[i].data, case.dtype), ora.params[i], f"param[{i}]")
+        # against the reference's own (CPU) results
+        assert_state_close(to_numpy(opt.exp_avg[i], 0), g[f"exp_avg_{i}"], f"ref exp_avg[{i}]")
+        assert_state_close(to_numpy(opt.exp_avg_sq[i], 0), g[f"exp_avg_sq_{i}"], f"ref exp_avg_sq[{i}]", max_ulp=3)
+        assert_state_close(to_numpy(opt.master[i], 0), g[f"master_{i}"], f"ref master[{i}]")
+    assert opt.step_count == case.steps
+
+
+def test_skip_decisions_match_reference():
+    for name, want in (("bf16_inf", math.isinf), ("bf16_nan", math.isnan)):
+        case = next(c for c in CASES if c.name == name)
+        params, opt = build(case)
+        norms = run_steps(case, params, opt, range(case.steps))
+        g = golden(name)["norms"]
+        assert [math.isfinite(x) for x in norms] == [bool(np.isfinite(x)) for x in g]
+        assert want(norms[1])
+
+
+def test_state_dict_round_trip_is_bit_identical():
+    import torch
+    from hybridagent_b200 import ZeroOneAdamW
+    case = next(c for c in CASES if c.name == "bf16_clip")
+    params, opt = build(case)
+    run_steps(case, params, opt, range(2))
+    sd = opt.state_dict()
+    fresh = [torch.nn.Parameter(p.detach().clone()) for p in params]
+    opt2 = ZeroOneAdamW([{"params": fresh, "lr": case.lr}], rank=0, world_size=1, betas=case.betas, eps=case.eps,
+                        weight_decay=case.weight_decay)
+    opt2.load_state_dict(sd)
+    assert opt2.step_count == 2 and dict(opt2.param_steps) == dict(opt.param_steps)
+    run_steps(case, params, opt, [2])
+    run_steps(case, fresh, opt2, [2])
+    for i in range(len(params)):
+        assert torch.equal(params[i].data, fresh[i].data)
+        for a, b in ((opt.master, opt2.master), (opt.exp_avg, opt2.exp_avg), (opt.exp_avg_sq, opt2.exp_avg_sq)):
+            assert torch.equal(a[i], b[i])
+    bad = dict(sd, world=2)
+    with pytest.raises(ValueError):
+        opt2.load_state_dict(bad)
+
+
+def test_pending_clip_semantics():
+    """apply_pending_clip scales the gradients exactly like the reference's in-place
+    mul_; a second clip_grad_norm sees the clipped gradients."""
+    import torch
+    case = next(c for c in CASES if c.name == "bf16_big_lr_clip")
+    params, opt = build(case)
+    grads = case.grads(0, 0)
+    for p, g, s in zip(params, grads, case.shapes):
+        p.grad = to_torch(g, case.dtype, s, "cuda")
+    n1 = opt.clip_grad_norm(1.0)
+    assert n1 > 1.0
+    opt.apply_pending_clip()
+    scale = 1.0 / (n1 + 1e-6)
+    for p, g in zip(params, grads):
+        want = g.copy()
+        Z.clip_inplace(want, case.dtype, Z.FORM_TORCH_CUDA, scale)
+        assert_bits_equal(to_numpy(p.grad, case.dtype), want, "clipped grad")
+    n2 = opt.clip_grad_norm(1.0)
+    assert abs(n2 - 1.0) < 1e-2
+    opt.zero_grad(set_to_none=False)
+    assert all(torch.count_nonzero(p.grad) == 0 for p in params)
+
+
+def test_constructor_contract():
+    import torch
+    from hybridagent_b200 import ZeroOneAdamW
+    p = torch.nn.Parameter(torch.zeros(8, device="cuda"))
+    with pytest.raises(ValueError, match="betas"):
+        ZeroOneAdamW([{"params": [p], "lr": 1e-3}], rank=0, world_size=1, betas=(0.9, 1.0))
+    with pytest.raises(ValueError, match="rank/world"):
+        ZeroOneAdamW([{"params": [p], "lr": 1e-3}], rank=1, world_size=1)
+    with pytest.raises(ValueError, match="no trainable"):
+        ZeroOneAdamW([{"params": [torch.zeros(3, device="cuda")], "lr": 1e-3}], rank=0, world_size=1)
+    with pytest.raises(RuntimeError, match="CUDA devices only"):
+        ZeroOneAdamW([{"params": [torch.nn.Parameter(torch.zeros(3))], "lr": 1e-3}], rank=0, world_size=1)
+    with pytest.raises(NotImplementedError):
+        ZeroOneAdamW([{"params": [p], "lr": 1e-3}], rank=0, world_size=1, use_8bit=True)
+    # duplicates and frozen parameters are dropped like optimizer.py:36-44
+    q = torch.nn.Parameter(torch.zeros(4, device="cuda"), requires_grad=False)
+    opt = ZeroOneAdamW([{"params": [p, p, q], "lr": 1e-3}, {"params": [p], "lr": 1.0}], rank=0, world_size=1)
+    assert len(opt.params) == 1 and opt.lrs == [1e-3]
+    assert opt.state_summary() == "ZeRO-1 FP32 AdamW: 1 tensors; rank 0 owns 0.0M parameters"
+
+
+def test_mixed_dtypes_and_strided_grads():
+    """bf16, fp16 and fp32 parameters in one optimizer (one launch per dtype class) with
+    non-contiguous gradients; every tensor bit for bit equal to the oracle."""
+    import torch
+    from hybridagent_b200 import ZeroOneAdamW
+    rng = np.random.default_rng(4)
+    spec = [((64, 96), Z.BF16), ((32,), Z.F32), ((100,), Z.BF16), ((48, 16), Z.F32), ((40, 24), Z.F16)]
+    init = [Z.narrow((rng.standard_normal(int(np.prod(s))) * 0.02).astype(np.float32), d) for s, d in spec]
+    params = [torch.nn.Parameter(to_torch(b, d, s, "cuda")) for b, (s, d) in zip(init, spec)]
+    opt = ZeroOneAdamW([{"params": params[:3], "lr": 1e-3}, {"params": params[3:], "lr": 3e-4}], rank=0,
+                       world_size=1, weight_decay=0.05)
+    ora = Z.OracleZeroOne(init, [d for _, d in spec], [1e-3, 1e-3, 1e-3, 3e-4, 3e-4], world=1, weight_decay=0.05)
+    for step in range(3):
+        grads = [Z.narrow((rng.standard_normal(int(np.prod(s))) * 0.3).astype(np.float32), d) for s, d in spec]
+        for p, g, (s, d) in zip(params, grads, spec):
+            t = to_torch(g, d, s, "cuda")
+            p.grad = t.t().contiguous().t() if len(s) == 2 else t  # column-major storage, same values
+            assert len(s) == 1 or not p.grad.is_contiguous()
+        norm = opt.clip_grad_norm(1.0)
+        opt.step()
+        ora.reduce_grads([grads])
+        ora.clip_grad_norm(1.0, norm=norm)
+        ora.step()
+    for i, (s, d) in enumerate(spec):
+        master, m, v, _ = ora.tensor_state(i)
+        assert_bits_equal(to_numpy(opt.master[i], 0), master, f"master[{i}]")
+        assert_bits_equal(to_numpy(opt.exp_avg[i], 0), m, f"exp_avg[{i}]")
+        assert_bits_equal(to_numpy(opt.exp_avg_sq[i], 0), v, f"exp_avg_sq[{i}]")
+        assert_bits_equal(to_numpy(params[i].data, d), ora.params[i], f"param[{i}]")
