@@ -42,7 +42,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-ALGO_BYTES_ADAMW = {"bf16": 28, "f16": 28, "f32": 32}   # per owned parameter, per AdamW launch
+ALGO_BYTES_ADAMW = {"bf16": 28, "f16": 28, "f32": 28}   # per owned parameter, per AdamW launch
 ALGO_BYTES_SUMSQ = {"bf16": 2, "f16": 2, "f32": 4}
 FALLBACK_HBM_GBS = 6650.0
 TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "adamw_kernel_qwen3_8b.md")
