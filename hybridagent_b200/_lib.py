@@ -17,6 +17,7 @@ HA_OK, HA_ERR_INVALID, HA_ERR_CUDA, HA_ERR_NCCL, HA_ERR_UNSUPPORTED = 0, 1, 2, 3
 HA_F32, HA_BF16, HA_F16, HA_F64, HA_I32, HA_U8 = 0, 1, 2, 3, 4, 5
 HA_ADAMW_CHUNK = 16384
 HA_SUMSQ_CHUNK = 32768
+HA_NOALLOC_SUMSQ_MAX_CHUNKS = 262144
 
 # numpy mirrors of the C structs (layouts asserted against the header's sizes)
 TENSOR_DTYPE = np.dtype([("grad", "<u8"), ("master", "<u8"), ("exp_avg", "<u8"), ("exp_avg_sq", "<u8"),
@@ -56,6 +57,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "ha_adamw_step": ([_vp, _vp, _i64, _i64, ctypes.c_int, ctypes.c_int, ctypes.POINTER(AdamwScalars), _vp],
                       ctypes.c_int),
     "ha_grad_sumsq": ([_vp, _vp, _i64, _i64, ctypes.c_int, _vp, _vp, _vp], ctypes.c_int),
+    "ha_grad_sumsq_noalloc": ([_vp, _vp, _i64, _i64, ctypes.c_int, _vp, _vp], ctypes.c_int),
     "ha_scale_grads": ([_vp, _vp, _i64, _i64, ctypes.c_int, _f32, _vp], ctypes.c_int),
     "ha_gather": ([_vp, _vp, _i64, _i64, ctypes.c_int, _vp], ctypes.c_int),
     "ha_comm_unique_id": ([_vp], ctypes.c_int),

@@ -11,6 +11,8 @@
 // depends only on the data and HA_SUMSQ_CHUNK, not on scheduling, and is far closer to
 // the exact sum than the reference's fp32 accumulation.  NaN and Inf propagate, so a
 // non-finite gradient anywhere makes the sum non-finite (the caller's skip decision).
+#include <mutex>
+
 #include "ha_common.cuh"
 
 namespace ha {
@@ -156,4 +158,79 @@ extern "C" int ha_grad_sumsq(const ha_tensor* d_tensors, const ha_chunk* d_chunk
   }
   finalize_kernel<<<1, kFinalThreads, 0, st>>>(d_partials, n_chunks, d_out);
   return check_launch("sumsq_finalize_kernel");
+}
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free variant of ha_grad_sumsq.
+//
+// Some callers cannot hand us a scratch buffer: an engine that has already reserved
+// nearly all of HBM for its own pools (a cudaMalloc of a few MB then fails or forces its
+// allocator to release cached blocks), a latency-critical loop that must not make the
+// implicitly synchronizing cudaMalloc / cudaFree calls, or a host binding with no device
+// allocator of its own.  For them the per-chunk fp64 partials live in the fixed array
+// below, reserved once in every GPU that loads this library and held until the process
+// exits: HA_NOALLOC_SUMSQ_MAX_CHUNKS doubles (2 MiB), enough for 8.59e9 elements per call.
+//
+// The host-side name of a __device__ array is not a device address, so the address is
+// looked up with cudaGetSymbolAddress the first time the entry point runs on each device
+// (with that device current) and cached.  Every call shares the one array: two calls
+// whose kernels overlap on the GPU (different streams, or different host threads) race on
+// it.  Each call writes every partial before reading it, so stale contents left by an
+// earlier call never reach a result and nothing needs clearing first.
+static __device__ __align__(256) double ha_noalloc_sumsq_partials[HA_NOALLOC_SUMSQ_MAX_CHUNKS];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+double* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the partials array on the current device (looked up once per device).
+int noalloc_partials(double** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return ha::fail(HA_ERR_CUDA, "ha_grad_sumsq_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return ha::fail(HA_ERR_UNSUPPORTED, "ha_grad_sumsq_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, ha_noalloc_sumsq_partials);
+    if (e != cudaSuccess || p == nullptr)
+      return ha::fail(HA_ERR_CUDA, "ha_grad_sumsq_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<double*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return HA_OK;
+}
+}  // namespace
+
+extern "C" int ha_grad_sumsq_noalloc(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,
+                                     int64_t chunk_elems, int grad_dtype, double* d_out, void* stream) {
+  using namespace ha;
+  if (chunk_elems != HA_SUMSQ_CHUNK)
+    return fail(HA_ERR_INVALID, "ha_grad_sumsq_noalloc: chunk_elems must be %d", HA_SUMSQ_CHUNK);
+  if (!valid_float_dtype(grad_dtype)) return fail(HA_ERR_UNSUPPORTED, "ha_grad_sumsq_noalloc: grad dtype %d", grad_dtype);
+  if (n_chunks < 0 || n_chunks > HA_NOALLOC_SUMSQ_MAX_CHUNKS)
+    return fail(HA_ERR_INVALID,
+                "ha_grad_sumsq_noalloc: %lld chunks exceed the fixed scratch of %d chunks (%lld elements); "
+                "use ha_grad_sumsq with a caller-allocated partials buffer",
+                (long long)n_chunks, HA_NOALLOC_SUMSQ_MAX_CHUNKS,
+                (long long)HA_NOALLOC_SUMSQ_MAX_CHUNKS * HA_SUMSQ_CHUNK);
+  if (d_out == nullptr) return fail(HA_ERR_INVALID, "ha_grad_sumsq_noalloc: NULL output");
+  if (n_chunks > 0 && (d_tensors == nullptr || d_chunks == nullptr))
+    return fail(HA_ERR_INVALID, "ha_grad_sumsq_noalloc: NULL table");
+  double* partials = nullptr;
+  if (int rc = noalloc_partials(&partials)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n_chunks > 0) {
+    const dim3 grid(static_cast<unsigned>(n_chunks));
+    switch (grad_dtype) {
+      case HA_F32: sumsq_kernel<HA_F32><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, partials); break;
+      case HA_BF16: sumsq_kernel<HA_BF16><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, partials); break;
+      default: sumsq_kernel<HA_F16><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, partials); break;
+    }
+    const int rc = check_launch("sumsq_kernel (noalloc)");
+    if (rc != HA_OK) return rc;
+  }
+  finalize_kernel<<<1, kFinalThreads, 0, st>>>(partials, n_chunks, d_out);
+  return check_launch("sumsq_finalize_kernel (noalloc)");
 }

@@ -143,6 +143,19 @@ int ha_adamw_step(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t 
 int ha_grad_sumsq(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks, int64_t chunk_elems,
                   int grad_dtype, double* d_partials, double* d_out, void* stream);
 
+/* Allocation-free ha_grad_sumsq, for callers that cannot allocate device scratch (an
+ * engine whose pools already hold nearly all of HBM, a loop that must avoid the implicit
+ * synchronization of cudaMalloc / cudaFree, a host binding without a device allocator).
+ * No counterpart in the reference.  The per-chunk partials live in a fixed array inside
+ * the library, reserved on every GPU that loads it until exit; n_chunks above
+ * HA_NOALLOC_SUMSQ_MAX_CHUNKS is rejected with HA_ERR_INVALID.  The first call on a device
+ * looks up that array's device address (with the device current) and caches it; make
+ * that first call before any stream capture.  All calls share the array: calls whose
+ * kernels overlap on the GPU race.  Same result as ha_grad_sumsq, bit for bit. */
+#define HA_NOALLOC_SUMSQ_MAX_CHUNKS 262144
+int ha_grad_sumsq_noalloc(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,
+                          int64_t chunk_elems, int grad_dtype, double* d_out, void* stream);
+
 /* In-place grad.mul_(scale) over the listed chunks, rounding to grad_dtype
  * (optimizer.py:157-159); mult is ha_adamw_scalars.clip_mult. */
 int ha_scale_grads(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks, int64_t chunk_elems,
