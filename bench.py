@@ -103,6 +103,8 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # one CPU measurement per job, on rank 0
+    import torch
+    torch.set_num_threads(len(os.sched_getaffinity(0)))  # torchrun sets OMP_NUM_THREADS=1; use every host core
     base = cpu_baseline(args.workload, args.cpu_sample_params, steps=min(max(args.steps, 1), 4), warmup=1)
     out = {"metric": "ZeRO-1 AdamW step Gparams/s", "value": base["value"], "unit": "Gparams/s",
            "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
