@@ -73,6 +73,7 @@ def cpu_baseline(workload: str, sample_params: int, steps: int = 4, warmup: int 
     from hybridagent_b200 import workloads
     from oracle.torch_ops import TorchZeroOneW1
 
+    torch.set_num_threads(len(os.sched_getaffinity(0)))  # every host core (torchrun would leave 1)
     shapes = workloads.truncated(workloads.WORKLOADS[workload](), sample_params)
     n = sum(math.prod(s) for s in shapes)
     g = torch.Generator().manual_seed(7)
@@ -103,8 +104,6 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # one CPU measurement per job, on rank 0
-    import torch
-    torch.set_num_threads(len(os.sched_getaffinity(0)))  # torchrun sets OMP_NUM_THREADS=1; use every host core
     base = cpu_baseline(args.workload, args.cpu_sample_params, steps=min(max(args.steps, 1), 4), warmup=1)
     out = {"metric": "ZeRO-1 AdamW step Gparams/s", "value": base["value"], "unit": "Gparams/s",
            "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,

@@ -18,6 +18,8 @@ HA_F32, HA_BF16, HA_F16, HA_F64, HA_I32, HA_U8 = 0, 1, 2, 3, 4, 5
 HA_ADAMW_CHUNK = 16384
 HA_SUMSQ_CHUNK = 32768
 HA_NOALLOC_SUMSQ_MAX_CHUNKS = 262144
+HA_SUM_REGIONS_CHUNK = 16384
+HA_MAX_PEERS = 15
 
 # numpy mirrors of the C structs (layouts asserted against the header's sizes)
 TENSOR_DTYPE = np.dtype([("grad", "<u8"), ("master", "<u8"), ("exp_avg", "<u8"), ("exp_avg_sq", "<u8"),
@@ -32,6 +34,10 @@ class AdamwScalars(ctypes.Structure):
     _fields_ = [("b1", ctypes.c_float), ("a1", ctypes.c_float), ("b2", ctypes.c_float), ("a2", ctypes.c_float),
                 ("eps", ctypes.c_float), ("use_decay", ctypes.c_int32), ("clip", ctypes.c_int32),
                 ("clip_mult", ctypes.c_float)]
+
+
+class Peers(ctypes.Structure):
+    _fields_ = [("n", ctypes.c_int32), ("reserved", ctypes.c_int32), ("delta", ctypes.c_int64 * 15)]
 
 
 class HAError(RuntimeError):
@@ -60,6 +66,15 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "ha_grad_sumsq_noalloc": ([_vp, _vp, _i64, _i64, ctypes.c_int, _vp, _vp], ctypes.c_int),
     "ha_scale_grads": ([_vp, _vp, _i64, _i64, ctypes.c_int, _f32, _vp], ctypes.c_int),
     "ha_gather": ([_vp, _vp, _i64, _i64, ctypes.c_int, _vp], ctypes.c_int),
+    "ha_malloc": ([_sz, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "ha_free": ([_vp], ctypes.c_int),
+    "ha_memset": ([_vp, ctypes.c_int, _sz, _vp], ctypes.c_int),
+    "ha_ipc_get_handle": ([_vp, _vp], ctypes.c_int),
+    "ha_ipc_open": ([_vp, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "ha_ipc_close": ([_vp], ctypes.c_int),
+    "ha_sum_regions": ([_vp, _i32, _i32, _i64, _i64, ctypes.c_int, _vp, _vp, _vp], ctypes.c_int),
+    "ha_adamw_step_peers": ([_vp, _vp, _i64, _i64, ctypes.c_int, ctypes.c_int, ctypes.POINTER(AdamwScalars),
+                             ctypes.POINTER(Peers), _vp], ctypes.c_int),
     "ha_comm_unique_id": ([_vp], ctypes.c_int),
     "ha_comm_init": ([_vp, _i32, _i32, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "ha_comm_destroy": ([_vp], ctypes.c_int),

@@ -26,7 +26,7 @@ LIB_PATH = os.path.join(LIB_DIR, "libhybridagent_b200.so")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["adamw.cu", "gradnorm.cu", "gather.cu"]
+CU_SOURCES = ["adamw.cu", "gradnorm.cu", "gather.cu", "p2p.cu"]
 CPP_SOURCES = ["host.cpp", "comm.cpp"]
 
 

@@ -50,11 +50,49 @@ __device__ __forceinline__ float grad_in(const Scalars& s, float g) {
   return s.clip ? clip_round<DT>(g, s.clip_mult) : g;
 }
 
+struct Peers {
+  int n;
+  int64_t delta[HA_MAX_PEERS];
+};
+
+// The new parameter value of 4 elements at local address `local` also goes to every peer.
+template <int DT, bool PEERS>
+__device__ __forceinline__ void push4(const Peers& p, uint64_t local, int64_t e, float4 x) {
+  if constexpr (PEERS) {
+#pragma unroll
+    for (int q = 0; q < HA_MAX_PEERS; ++q) {  // constant indices keep delta[] in the parameter bank
+      if (q >= p.n) break;
+      void* dst = reinterpret_cast<void*>(local + p.delta[q]);
+      if constexpr (DT == HA_F32) {
+        store4_f32(static_cast<float*>(dst), e, x);
+      } else {
+        store4_narrow<DT>(dst, e, x);
+      }
+    }
+  }
+}
+
+template <int DT, bool PEERS>
+__device__ __forceinline__ void push1(const Peers& p, uint64_t local, int64_t k, float x) {
+  if constexpr (PEERS) {
+#pragma unroll
+    for (int q = 0; q < HA_MAX_PEERS; ++q) {
+      if (q >= p.n) break;
+      if constexpr (DT == HA_F32) {
+        reinterpret_cast<float*>(local + p.delta[q])[k] = x;
+      } else {
+        reinterpret_cast<uint16_t*>(local + p.delta[q])[k] = Elem<DT>::narrow(x);
+      }
+    }
+  }
+}
+
 // DT is the gradient and parameter dtype.  For HA_F32 the master is the parameter
-// (optimizer.py:71-73) and no separate copy is written.
-template <int DT>
+// (optimizer.py:71-73) and no separate copy is written.  PEERS: the new parameter values
+// are also stored into every peer's copy of the packed parameter buffer.
+template <int DT, bool PEERS>
 __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __restrict__ tensors,
-                                                         const ha_chunk* __restrict__ chunks, Scalars s) {
+                                                         const ha_chunk* __restrict__ chunks, Scalars s, Peers peers) {
   __shared__ StagedChunk sc;
   stage_chunk(tensors, chunks, &sc);
   const ha_tensor& t = sc.t;
@@ -67,6 +105,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
   float* exp_avg_sq = reinterpret_cast<float*>(t.exp_avg_sq);
   void* param = reinterpret_cast<void*>(t.param);
   const float decay = t.decay, neg_lr = t.neg_lr, rc1 = t.rc1, rc2 = t.rc2;
+  const uint64_t pushed = DT == HA_F32 ? t.master : t.param;  // the parameter's local address
 
   constexpr uint64_t kNarrowAlign = DT == HA_F32 ? 15 : 7;
   const bool vec = ((t.master | t.exp_avg | t.exp_avg_sq) & 15) == 0 && (t.grad & kNarrowAlign) == 0 &&
@@ -96,6 +135,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
           store4_f32(exp_avg, e[u], m[u]);
           store4_f32(exp_avg_sq, e[u], v[u]);
           if constexpr (DT != HA_F32) store4_narrow<DT>(param, e[u], ms[u]);
+          push4<DT, PEERS>(peers, pushed, e[u], ms[u]);
         } else {
           for (int64_t k = e[u]; k < end; ++k) {  // ragged tail of the tensor (one thread)
             float a = master[k], b = exp_avg[k], c = exp_avg_sq[k];
@@ -104,6 +144,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
             exp_avg[k] = b;
             exp_avg_sq[k] = c;
             if constexpr (DT != HA_F32) static_cast<uint16_t*>(param)[k] = Elem<DT>::narrow(a);
+            push1<DT, PEERS>(peers, pushed, k, a);
           }
         }
       }
@@ -116,6 +157,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
       exp_avg[k] = b;
       exp_avg_sq[k] = c;
       if constexpr (DT != HA_F32) static_cast<uint16_t*>(param)[k] = Elem<DT>::narrow(a);
+      push1<DT, PEERS>(peers, pushed, k, a);
     }
   }
 }
@@ -159,12 +201,44 @@ extern "C" int ha_adamw_step(const ha_tensor* d_tensors, const ha_chunk* d_chunk
   const Scalars s{sc->b1, sc->a1, sc->b2, sc->a2, sc->eps, sc->use_decay, sc->clip, sc->clip_mult};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid(static_cast<unsigned>(n_chunks));
+  const Peers none{};
   switch (grad_dtype) {
-    case HA_F32: adamw_kernel<HA_F32><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s); break;
-    case HA_BF16: adamw_kernel<HA_BF16><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s); break;
-    default: adamw_kernel<HA_F16><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s); break;
+    case HA_F32: adamw_kernel<HA_F32, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none); break;
+    case HA_BF16: adamw_kernel<HA_BF16, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none); break;
+    default: adamw_kernel<HA_F16, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none); break;
   }
   return check_launch("adamw_kernel");
+}
+
+extern "C" int ha_adamw_step_peers(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,
+                                   int64_t chunk_elems, int grad_dtype, int param_dtype, const ha_adamw_scalars* sc,
+                                   const ha_peers* peers, void* stream) {
+  using namespace ha;
+  if (chunk_elems != HA_ADAMW_CHUNK)
+    return fail(HA_ERR_INVALID, "ha_adamw_step_peers: chunk_elems must be %d", HA_ADAMW_CHUNK);
+  if (!valid_float_dtype(grad_dtype)) return fail(HA_ERR_UNSUPPORTED, "ha_adamw_step_peers: grad dtype %d", grad_dtype);
+  if (grad_dtype != HA_F32 && param_dtype != grad_dtype)
+    return fail(HA_ERR_UNSUPPORTED, "ha_adamw_step_peers: param dtype %d with grad dtype %d", param_dtype, grad_dtype);
+  if (n_chunks < 0 || n_chunks > 0x7fffffffLL)
+    return fail(HA_ERR_INVALID, "ha_adamw_step_peers: n_chunks %lld", (long long)n_chunks);
+  if (sc == nullptr || peers == nullptr) return fail(HA_ERR_INVALID, "ha_adamw_step_peers: NULL scalars or peers");
+  if (peers->n < 0 || peers->n > HA_MAX_PEERS) return fail(HA_ERR_INVALID, "ha_adamw_step_peers: %d peers", peers->n);
+  for (int q = 0; q < peers->n; ++q)
+    if ((peers->delta[q] & 15) != 0) return fail(HA_ERR_INVALID, "ha_adamw_step_peers: peer %d offset not 16-byte aligned", q);
+  if (n_chunks == 0) return HA_OK;
+  if (d_tensors == nullptr || d_chunks == nullptr) return fail(HA_ERR_INVALID, "ha_adamw_step_peers: NULL table");
+  const Scalars s{sc->b1, sc->a1, sc->b2, sc->a2, sc->eps, sc->use_decay, sc->clip, sc->clip_mult};
+  Peers p{};
+  p.n = peers->n;
+  for (int q = 0; q < peers->n; ++q) p.delta[q] = peers->delta[q];
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid(static_cast<unsigned>(n_chunks));
+  switch (grad_dtype) {
+    case HA_F32: adamw_kernel<HA_F32, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p); break;
+    case HA_BF16: adamw_kernel<HA_BF16, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p); break;
+    default: adamw_kernel<HA_F16, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p); break;
+  }
+  return check_launch("adamw_kernel (peers)");
 }
 
 extern "C" int ha_scale_grads(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,

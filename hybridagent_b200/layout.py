@@ -94,3 +94,61 @@ def chunk_table(numels: list[int], chunk_elems: int, include: list[bool] | None 
                   count.value, ctypes.byref(count))
         _lib.call("ha_check_chunks", n, _lib.np_ptr(sizes), _lib.np_ptr(out), count.value, chunk_elems)
     return out
+
+
+def push_destinations(cls: DtypeClass, owner: list[int], rank: int, elem_bytes: int,
+                      grad_bases: list[int] | None, local_grad_base: int) -> list[int]:
+    """Where this rank's gradient of every tensor of ``cls`` goes (bytes addresses).
+
+    p2p (``grad_bases`` = every rank's address of its receive buffer, as mapped here): into
+    the owner's buffer, region ``rank`` (rank r's contributions occupy elements
+    [r*seg_len, (r+1)*seg_len)), at the tensor's offset in the owner's segment -- so the
+    owner finds all ranks' copies of a tensor at the same offset of consecutive regions.
+    nccl (``grad_bases`` None): into the local owner-major pack, segment ``owner``, the
+    layout an equal-count reduce-scatter expects."""
+    out = []
+    for i in cls.indices:
+        if grad_bases is None:
+            out.append(local_grad_base + (owner[i] * cls.seg_len + cls.offset[i]) * elem_bytes)
+        else:
+            out.append(grad_bases[owner[i]] + (rank * cls.seg_len + cls.offset[i]) * elem_bytes)
+    return out
+
+
+def peer_deltas(param_bases: list[int], rank: int) -> list[int]:
+    """Byte offsets from this rank's packed parameter buffer to each peer's (rank order,
+    skipping this rank): the same element lives at the same offset on every rank."""
+    return [b - param_bases[rank] for r, b in enumerate(param_bases) if r != rank]
+
+
+def push_chunk_order(cls: DtypeClass, owner: list[int], rank: int, world: int, numels: list[int],
+                     chunk_elems: int) -> np.ndarray:
+    """ha_chunk list of the gradient push, interleaved across destination owners.
+
+    Chunks run roughly in list order, so a tensor-ordered list keeps every in-flight CTA on
+    one destination at a time: local copies and NVLink stores would not overlap, and since
+    every rank walks the tensors in the same order, all ranks would store into the same
+    owner at once and share its ingress.  Instead each round takes one chunk per owner,
+    starting at owner rank+1 and ending with this rank's own (local) tensors, so at any
+    moment every owner receives from every peer and the local copies run alongside."""
+    per_owner: list[list[tuple[int, int]]] = [[] for _ in range(world)]
+    for k, i in enumerate(cls.indices):
+        n_chunks = (numels[i] + chunk_elems - 1) // chunk_elems
+        per_owner[owner[i]].extend((k, c) for c in range(n_chunks))
+    order = [(rank + d) % world for d in range(1, world + 1)]
+    out = []
+    pos = [0] * world
+    remaining = sum(len(x) for x in per_owner)
+    while remaining:
+        for o in order:
+            if pos[o] < len(per_owner[o]):
+                out.append(per_owner[o][pos[o]])
+                pos[o] += 1
+                remaining -= 1
+    tab = np.zeros(len(out), dtype=_lib.CHUNK_DTYPE)
+    if out:
+        tab["tensor"] = [k for k, _ in out]
+        tab["index"] = [c for _, c in out]
+        sizes = np.ascontiguousarray([numels[i] for i in cls.indices], dtype=np.int64)
+        _lib.call("ha_check_chunks", len(cls.indices), _lib.np_ptr(sizes), _lib.np_ptr(tab), len(tab), chunk_elems)
+    return tab

@@ -10,15 +10,23 @@ reference              what it does there                             here
                        tensor                                         packed fp32 buffer per dtype class, and at
                                                                       world > 1 the parameters are re-homed into
                                                                       an owner-major packed buffer
-``all_reduce_grads``   used-mask MAX all-reduce; per owner, 64 Mi-    used-mask MAX (uint8, NCCL); one multi-tensor
-:95-143                element bf16 buckets packed, ``dist.reduce``,  pack kernel; ONE NCCL reduce-scatter; owned
-                       owner clones                                   grads become views of the reduced segment
-``clip_grad_norm``     per-tensor ``float().square().sum()``, fp32    one multi-tensor sum-of-squares kernel (fp64
-:145-160               all-reduce, ``float(sqrt)``, bf16 ``mul_``     partials, fixed order), one 8-byte NCCL
+``all_reduce_grads``   used-mask MAX all-reduce; per owner, 64 Mi-    used-mask MAX (uint8, NCCL); one push kernel
+:95-143                element bf16 buckets packed, ``dist.reduce``,  stores every gradient into its owner's receive
+                       owner clones                                   buffer over NVLink; the owner's sum kernel adds
+                                                                      the ranks' regions and emits the norm's square
+                                                                      sums; owned grads are views of the sum
+``clip_grad_norm``     per-tensor ``float().square().sum()``, fp32    the fused square sums (or one multi-tensor
+:145-160               all-reduce, ``float(sqrt)``, bf16 ``mul_``     sum-of-squares kernel), one 8-byte NCCL
                                                                       all-reduce; the clip is folded into ``step``
 ``step`` :162-194      ~13 eager kernels per tensor, then one         one fused AdamW kernel per dtype class (28
-                       ``dist.broadcast`` per tensor                  B/param for bf16), ONE NCCL all-gather
+                       ``dist.broadcast`` per tensor                  B/param for bf16) that also stores each new
+                                                                      parameter into every peer's copy
 =====================  =============================================  ==========================================
+
+At world size > 1 the ranks map each other's packed buffers with CUDA IPC ("p2p" mode,
+the default).  If any rank cannot map a peer, every rank uses "nccl" mode instead: a local
+pack kernel, an NCCL reduce-scatter and an NCCL all-gather over the same buffers.  The
+environment variable HYBRIDAGENT_B200_COMM=nccl selects that mode explicitly.
 
 Numerics: every element is updated with the rounding torch's CUDA kernels give the
 reference's op sequence, so master / exp_avg / exp_avg_sq and the parameter copy equal
@@ -36,21 +44,27 @@ Deliberate differences (documented surface):
   ``clip_grad_norm`` or an ``all_reduce_grads`` before ``step`` applies it first, so
   chained calls see exactly the reference's values.
 * At world_size > 1 ``param.data`` of every parameter is re-bound at construction to a
-  view of the packed parameter buffer (values unchanged) so the all-gather writes the
-  model's weights in place; parameters must not be re-bound afterwards.
+  view of the packed parameter buffer (each tensor takes its owner's values, as the
+  reference's broadcast would) so the all-gather writes the model's weights in place;
+  parameters must not be re-bound afterwards.
+* At world_size > 1 in p2p mode the norm's square sums come out of ``all_reduce_grads``;
+  ``clip_grad_norm`` recomputes them if an owned ``p.grad`` was replaced in between, but
+  not if one was modified in place (the reference's trainer does neither).
 * ``use_8bit=True`` (bitsandbytes PagedAdamW8bit, optimizer.py:76-86) is not provided.
 * ``state_dict`` / ``load_state_dict`` are new (the reference has neither).
 """
 from __future__ import annotations
 
 import ctypes
+import os
 from collections.abc import MutableMapping
 
 import numpy as np
 import torch
 
 from . import _lib, layout
-from ._lib import HA_ADAMW_CHUNK, HA_BF16, HA_F16, HA_F32, HA_F64, HA_SUMSQ_CHUNK, HA_U8
+from ._lib import (HA_ADAMW_CHUNK, HA_BF16, HA_F16, HA_F32, HA_F64, HA_I32, HA_SUM_REGIONS_CHUNK, HA_SUMSQ_CHUNK,
+                   HA_U8)
 
 _CODES = {torch.float32: HA_F32, torch.bfloat16: HA_BF16, torch.float16: HA_F16}
 _TORCH = {v: k for k, v in _CODES.items()}
@@ -133,11 +147,14 @@ class _Class:
         dev = opt.device
         W, r = opt.world, opt.rank
         numel = opt._numels
-        # --- packed parameter / gradient buffers (world > 1)
+        # --- packed parameter / gradient buffers (world > 1), IPC-shareable
         self.packed_param = self.packed_grad = None
         if W > 1:
-            self.packed_param = torch.empty(W * cls.seg_len, dtype=self.dtype, device=dev)
-            self.packed_grad = torch.zeros(W * cls.seg_len, dtype=self.dtype, device=dev)
+            from .p2p import DeviceBuffer
+            self.param_buf = DeviceBuffer(W * cls.seg_len, self.dtype, dev)
+            self.grad_buf = DeviceBuffer(W * cls.seg_len, self.dtype, dev)
+            self.packed_param = self.param_buf.tensor
+            self.packed_grad = self.grad_buf.tensor
             for i in cls.indices:
                 p = opt.params[i]
                 start = opt.owner[i] * cls.seg_len + cls.offset[i]
@@ -175,24 +192,40 @@ class _Class:
         self.adamw_chunks = self._device_chunks(owned_numels, HA_ADAMW_CHUNK, dev)
         self.sumsq_chunks = self._device_chunks(owned_numels, HA_SUMSQ_CHUNK, dev)
         self.partials = torch.empty(max(self.sumsq_chunks[1], 1), dtype=torch.float64, device=dev)
-        # --- pack table (world > 1): every tensor of the class -> its slot in packed_grad
-        self.pack = None
+        # --- gradient move table (world > 1): every tensor of the class -> where this rank's
+        # gradient goes (p2p: the owner's receive region of this rank; nccl: its slot in the
+        # local owner-major pack); destinations are set by set_destinations()
+        self.move = None
         if W > 1:
-            self.pack = _Table(len(cls.indices), _lib.COPY_DTYPE, dev)
-            cp = self.pack.np
-            base = self.packed_grad.data_ptr()
-            esz = self.packed_grad.element_size()
-            self.slot_ptr = {}
+            self.move = _Table(len(cls.indices), _lib.COPY_DTYPE, dev)
             for k, i in enumerate(cls.indices):
-                addr = base + (opt.owner[i] * cls.seg_len + cls.offset[i]) * esz
-                self.slot_ptr[i] = addr
-                cp[k]["dst"] = addr
-                cp[k]["numel"] = numel[i]
-            self.pack_chunks = self._device_chunks([numel[i] for i in cls.indices], HA_ADAMW_CHUNK, dev)
-            # reduced gradient views handed to the caller as p.grad (optimizer.py:141)
+                self.move.np[k]["numel"] = numel[i]
+            self.move_chunks = self._device_chunks([numel[i] for i in cls.indices], HA_ADAMW_CHUNK, dev)
+            # reduced gradients handed to the caller as p.grad (optimizer.py:141): the owner's own
+            # segment of the gradient buffer in both modes
             own0 = r * cls.seg_len
             self.grad_view = {i: self.packed_grad[own0 + cls.offset[i]:own0 + cls.offset[i] + numel[i]]
                               .view(opt.params[i].shape) for i in self.owned}
+            n_regions = max((cls.own_len[r] + HA_SUM_REGIONS_CHUNK - 1) // HA_SUM_REGIONS_CHUNK, 1)
+            self.region_partials = torch.empty(n_regions, dtype=torch.float64, device=dev)
+            self.peers = _lib.Peers()
+
+    def set_destinations(self, opt: "ZeroOneAdamW", grad_bases: list[int] | None,
+                         param_bases: list[int] | None) -> None:
+        """p2p when the peers' buffer addresses are given, else the local nccl pack."""
+        dst = layout.push_destinations(self.layout, opt.owner, opt.rank, self.packed_grad.element_size(),
+                                       grad_bases, self.packed_grad.data_ptr())
+        self.move.np["dst"][:len(dst)] = dst
+        if grad_bases is not None:  # p2p: interleave the push across destination owners
+            order = layout.push_chunk_order(self.layout, opt.owner, opt.rank, opt.world, opt._numels,
+                                            HA_ADAMW_CHUNK)
+            self.move_chunks = (torch.from_numpy(order.view(np.uint8).copy()).to(opt.device), len(order))
+        self.peers = _lib.Peers()
+        if param_bases is not None:
+            deltas = layout.peer_deltas(param_bases, opt.rank)
+            for q, d in enumerate(deltas):
+                self.peers.delta[q] = d
+            self.peers.n = len(deltas)
 
     @staticmethod
     def _device_chunks(numels: list[int], chunk: int, dev) -> tuple[torch.Tensor | None, int]:
@@ -258,16 +291,59 @@ class ZeroOneAdamW:
             self.param_steps = _ParamSteps(self._steps, owned_all)
             self.owned_numel = sum(self._numels[i] for i in owned_all)
             self._comm = None
+            self._peer_map = None
+            self.comm_mode = "local"
             if self.world > 1:
                 from .comm import NcclComm
                 self._comm = NcclComm(self.rank, self.world)
             self._classes = [_Class(self, c) for c in self._plan.classes]
             self._norm_buf = torch.zeros(len(self._classes), dtype=torch.float64, device=self.device)
             self._used_dev = torch.zeros(len(self.params), dtype=torch.uint8, device=self.device)
+            self._barrier_buf = torch.zeros(1, dtype=torch.int32, device=self.device)
+            if self.world > 1:
+                self._setup_world()
             torch.cuda.current_stream().synchronize()
         self._pending_clip: float | None = None
+        self._fused_sumsq: list | None = None
         self.timer = None  # optional phase timer: .begin(name) / .end(name) around kernel launches
         self.launches = 0  # kernels of libhybridagent_b200 launched so far
+
+    def _setup_world(self) -> None:
+        """Owners' parameter values to every rank (the reference's broadcast), then the
+        peer mappings (p2p) or the nccl fallback, chosen identically on every rank."""
+        for c in self._classes:
+            own = c.packed_param.data_ptr() + self.rank * c.layout.seg_len * c.packed_param.element_size()
+            self._comm.all_gather(own, c.packed_param.data_ptr(), c.layout.seg_len, c.code)
+        want = os.environ.get("HYBRIDAGENT_B200_COMM", "p2p")
+        if want not in ("p2p", "nccl"):
+            raise ValueError(f"HYBRIDAGENT_B200_COMM={want!r}: expected p2p or nccl")
+        ok = 0
+        if want == "p2p":
+            from .p2p import PeerMap
+            bufs = {}
+            for k, c in enumerate(self._classes):
+                bufs[f"grad{k}"] = c.grad_buf
+                bufs[f"param{k}"] = c.param_buf
+            self._peer_map = PeerMap(bufs, self.rank, self.world)
+            ok = 1 if self._peer_map.ok else 0
+        flag = torch.tensor([1 - ok], dtype=torch.int32, device=self.device)
+        self._comm.all_reduce_max(flag, HA_I32)  # every rank takes the same mode
+        use_p2p = int(flag.item()) == 0
+        if not use_p2p and self._peer_map is not None:
+            self._peer_map.close()
+            self._peer_map = None
+        self.comm_mode = "p2p" if use_p2p else "nccl"
+        for k, c in enumerate(self._classes):
+            if use_p2p:
+                c.set_destinations(self, self._peer_map.bases[f"grad{k}"], self._peer_map.bases[f"param{k}"])
+            else:
+                c.set_destinations(self, None, None)
+            c.move.upload()
+
+    def _barrier(self) -> None:
+        """Stream-ordered barrier across ranks: returns on every rank's stream only after every
+        rank's earlier work (this rank's peer stores included) has completed."""
+        self._comm.all_reduce_sum(self._barrier_buf, HA_I32)
 
     # ---------------------------------------------------------------- helpers
     def _phase(self, name: str, start: bool) -> None:
@@ -311,6 +387,7 @@ class ZeroOneAdamW:
     def zero_grad(self, set_to_none: bool = True) -> None:
         """optimizer.py:88-93."""
         self._pending_clip = None
+        self._fused_sumsq = None
         for parameter in self.params:
             if set_to_none:
                 parameter.grad = None
@@ -330,9 +407,9 @@ class ZeroOneAdamW:
             self._used_dev.copy_(torch.from_numpy(local), non_blocking=False)
             self._comm.all_reduce_max(self._used_dev, HA_U8)
             used = self._used_dev.cpu().numpy().astype(bool)
-            keep = []  # gradients that must stay alive until the pack kernel has read them
+            keep = []  # gradients that must stay alive until the move kernel has read them
             for c in self._classes:
-                cp = c.pack.np
+                cp = c.move.np
                 for k, i in enumerate(c.layout.indices):
                     p = self.params[i]
                     if p.data.data_ptr() != c.packed_param.data_ptr() + (
@@ -340,24 +417,39 @@ class ZeroOneAdamW:
                         raise RuntimeError(f"parameter {i} was re-bound after the optimizer was built")
                     g = p.grad
                     if g is None or not used[i]:
-                        cp[k]["src"] = 0
+                        cp[k]["src"] = 0  # contributes zeros (optimizer.py:131-132)
                         continue
-                    if g.dtype != c.dtype or g.numel() != self._numels[i]:
-                        raise RuntimeError(f"gradient of tensor {i}: {g.dtype} x {g.numel()}")
+                    if g.dtype != c.dtype or g.numel() != self._numels[i] or g.device != self.device:
+                        raise RuntimeError(f"gradient of tensor {i}: {g.dtype} x {g.numel()} on {g.device}")
                     if not g.is_contiguous():
                         g = g.contiguous()
                     keep.append(g)
                     cp[k]["src"] = g.data_ptr()  # equal to dst when the gradient already lives in its slot
-                c.pack.upload()
-                self._phase("pack", True)
-                if c.pack_chunks[1]:
-                    _lib.call("ha_gather", c.pack.ptr, c.pack_chunks[0].data_ptr(), c.pack_chunks[1], HA_ADAMW_CHUNK,
+                c.move.upload()
+            p2p = self.comm_mode == "p2p"
+            self._phase("push" if p2p else "pack", True)
+            for c in self._classes:
+                if c.move_chunks[1]:
+                    _lib.call("ha_gather", c.move.ptr, c.move_chunks[0].data_ptr(), c.move_chunks[1], HA_ADAMW_CHUNK,
                               c.packed_grad.element_size(), self._stream())
                     self.launches += 1
-                self._phase("pack", False)
+            self._phase("push" if p2p else "pack", False)
+            if p2p:
+                self._phase("barrier", True)
+                self._barrier()  # every rank's pushes have landed
+                self._phase("barrier", False)
+                self._phase("sum_regions", True)
+                for k, c in enumerate(self._classes):
+                    _lib.call("ha_sum_regions", c.grad_buf.ptr, self.world, self.rank, c.layout.seg_len,
+                              c.layout.own_len[self.rank], c.code, c.region_partials.data_ptr(),
+                              self._norm_buf[k:].data_ptr(), self._stream())
+                    self.launches += 2 if c.layout.own_len[self.rank] else 1
+                self._phase("sum_regions", False)
+            else:
                 self._phase("reduce_scatter", True)
-                own = c.packed_grad.data_ptr() + self.rank * c.layout.seg_len * c.packed_grad.element_size()
-                self._comm.reduce_scatter(c.packed_grad.data_ptr(), own, c.layout.seg_len, c.code)
+                for c in self._classes:
+                    own = c.packed_grad.data_ptr() + self.rank * c.layout.seg_len * c.packed_grad.element_size()
+                    self._comm.reduce_scatter(c.packed_grad.data_ptr(), own, c.layout.seg_len, c.code)
                 self._phase("reduce_scatter", False)
             del keep
             for c in self._classes:
@@ -366,6 +458,9 @@ class ZeroOneAdamW:
                         self.params[i].grad = c.grad_view[i]
                     else:
                         self.params[i].grad = None
+            # the square sums of exactly these gradients are ready (p2p): clip_grad_norm reuses
+            # them unless an owned gradient is replaced before it runs
+            self._fused_sumsq = [self.params[i].grad for c in self._classes for i in c.owned] if p2p else None
 
     @torch.no_grad()
     def clip_grad_norm(self, max_norm: float) -> float:
@@ -373,19 +468,24 @@ class ZeroOneAdamW:
         (optimizer.py:145-160).  Returns the pre-clip norm."""
         self.apply_pending_clip()
         with torch.cuda.device(self.device):
-            keep = []  # contiguous copies of strided gradients must outlive the launches
-            for c in self._classes:
-                grads, ptrs = self._owned_grads(c)
-                keep.append(grads)
-                self._upload_table(c, ptrs, advance=False)
-            self._phase("sumsq", True)
-            for k, c in enumerate(self._classes):
-                chunks, n = c.sumsq_chunks
-                _lib.call("ha_grad_sumsq", c.table.ptr, None if chunks is None else chunks.data_ptr(), n,
-                          HA_SUMSQ_CHUNK, c.code, c.partials.data_ptr(), self._norm_buf[k:].data_ptr(),
-                          self._stream())
-                self.launches += 2 if n else 1
-            self._phase("sumsq", False)
+            fused = self._fused_sumsq
+            self._fused_sumsq = None
+            reuse = fused is not None and all(
+                self.params[i].grad is g for g, i in zip(fused, (i for c in self._classes for i in c.owned)))
+            if not reuse:
+                keep = []  # contiguous copies of strided gradients must outlive the launches
+                for c in self._classes:
+                    grads, ptrs = self._owned_grads(c)
+                    keep.append(grads)
+                    self._upload_table(c, ptrs, advance=False)
+                self._phase("sumsq", True)
+                for k, c in enumerate(self._classes):
+                    chunks, n = c.sumsq_chunks
+                    _lib.call("ha_grad_sumsq", c.table.ptr, None if chunks is None else chunks.data_ptr(), n,
+                              HA_SUMSQ_CHUNK, c.code, c.partials.data_ptr(), self._norm_buf[k:].data_ptr(),
+                              self._stream())
+                    self.launches += 2 if n else 1
+                self._phase("sumsq", False)
             if self.world > 1:
                 self._comm.all_reduce_sum(self._norm_buf, HA_F64)
             partial = self._norm_buf.cpu().tolist()
@@ -402,6 +502,7 @@ class ZeroOneAdamW:
         if self._pending_clip is None:
             return
         scale, self._pending_clip = self._pending_clip, None
+        self._fused_sumsq = None  # the gradients change below
         with torch.cuda.device(self.device):
             keep = []
             for c in self._classes:
@@ -433,15 +534,24 @@ class ZeroOneAdamW:
                 _lib.call("ha_make_scalars", self.betas[0], self.betas[1], self.eps, self.weight_decay, c.code,
                           0 if scale is None else 1, 0.0 if scale is None else scale, ctypes.byref(sc))
                 launches.append((c, sc))
+            p2p = self.comm_mode == "p2p"
             self._phase("adamw", True)
             for c, sc in launches:
                 chunks, n = c.adamw_chunks
-                if n:
+                if n and p2p:  # the update also writes each new parameter into every peer's copy
+                    _lib.call("ha_adamw_step_peers", c.table.ptr, chunks.data_ptr(), n, HA_ADAMW_CHUNK, c.code,
+                              c.code, ctypes.byref(sc), ctypes.byref(c.peers), self._stream())
+                    self.launches += 1
+                elif n:
                     _lib.call("ha_adamw_step", c.table.ptr, chunks.data_ptr(), n, HA_ADAMW_CHUNK, c.code, c.code,
                               ctypes.byref(sc), self._stream())
                     self.launches += 1
             self._phase("adamw", False)
-            if self.world > 1:
+            if p2p:
+                self._phase("barrier", True)
+                self._barrier()  # peers use their parameters only after every rank's stores landed
+                self._phase("barrier", False)
+            elif self.world > 1:
                 self._phase("all_gather", True)
                 for c in self._classes:
                     own = c.packed_param.data_ptr() + self.rank * c.layout.seg_len * c.packed_param.element_size()
@@ -502,7 +612,12 @@ class ZeroOneAdamW:
         torch.cuda.current_stream(self.device).synchronize()
 
     def close(self) -> None:
-        """Releases the NCCL communicator (world_size > 1)."""
+        """Releases the peer mappings and the NCCL communicator (world_size > 1).  Call it on
+        every rank after the last step."""
+        if self._peer_map is not None:
+            torch.cuda.current_stream(self.device).synchronize()
+            self._peer_map.close()
+            self._peer_map = None
         if self._comm is not None:
             self._comm.close()
             self._comm = None

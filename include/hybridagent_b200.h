@@ -45,6 +45,11 @@ extern "C" {
 /* Elements per chunk of the multi-tensor kernels: one CTA processes one chunk. */
 #define HA_ADAMW_CHUNK 16384
 #define HA_SUMSQ_CHUNK 32768
+#define HA_SUM_REGIONS_CHUNK 16384
+
+/* Largest number of peers a rank can push to (an NVLink domain of 16 GPUs). */
+#define HA_MAX_PEERS 15
+#define HA_IPC_HANDLE_BYTES 64
 
 const char* ha_last_error(void);
 int ha_abi_version(void);
@@ -165,6 +170,43 @@ int ha_scale_grads(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t
  * chunk_elems elements of elem_bytes (2 or 4) per chunk. */
 int ha_gather(const ha_copy* d_copies, const ha_chunk* d_chunks, int64_t n_chunks, int64_t chunk_elems,
               int elem_bytes, void* stream);
+
+/* ------------------------------------------------------------------ peer-to-peer (NVLink / NVSwitch) */
+
+/* Byte offsets from this rank's packed parameter buffer to every peer's mapping of that
+ * peer's packed parameter buffer (same layout on all ranks). */
+typedef struct ha_peers {
+  int32_t n;                    /* number of peers (world - 1), at most HA_MAX_PEERS */
+  int32_t reserved;
+  int64_t delta[HA_MAX_PEERS];  /* peer address = local address + delta[q] */
+} ha_peers;
+
+/* Device memory that can be shared with other processes through CUDA IPC (the packed
+ * parameter and gradient-receive buffers of world > 1). */
+int ha_malloc(size_t bytes, void** out);
+int ha_free(void* ptr);
+int ha_memset(void* ptr, int value, size_t bytes, void* stream);
+int ha_ipc_get_handle(const void* ptr, uint8_t out[HA_IPC_HANDLE_BYTES]);
+int ha_ipc_open(const uint8_t handle[HA_IPC_HANDLE_BYTES], void** out);
+int ha_ipc_close(void* ptr);
+
+/* Owner side of the gradient reduction (replaces the dist.reduce of optimizer.py:136 and
+ * the norm's square-sum of :149-151 in one pass): d_regions holds `world` regions of
+ * region_elems elements, region r written by rank r's push (ha_gather into the owner's
+ * receive buffer).  Elements [0, count) of all regions are added in fp32 in rank order
+ * 0..world-1, rounded once to dtype and written over region `rank`; the sum of squares of
+ * the written values goes to d_partials (one per HA_SUM_REGIONS_CHUNK) and d_out[0].  At
+ * world 2 this equals any SUM reduction of the two gradients bit for bit. */
+int ha_sum_regions(void* d_regions, int32_t world, int32_t rank, int64_t region_elems, int64_t count, int dtype,
+                   double* d_partials, double* d_out, void* stream);
+
+/* ha_adamw_step that also stores every updated parameter value (the low-precision copy,
+ * or the fp32 master when the master is the parameter) at the same offset in each peer's
+ * packed parameter buffer: the parameter all-gather of optimizer.py:192-194 fused into the
+ * update.  The caller orders the peers' next reads after a collective. */
+int ha_adamw_step_peers(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,
+                        int64_t chunk_elems, int grad_dtype, int param_dtype, const ha_adamw_scalars* scalars,
+                        const ha_peers* peers, void* stream);
 
 /* ------------------------------------------------------------------ NCCL (NVLink / NVSwitch) */
 

@@ -35,3 +35,33 @@ def test_mixed_dtype_classes():
     for c in p.classes:
         for r in range(2):
             assert c.own_len[r] <= c.seg_len
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_push_chunk_order_covers_every_chunk_once_and_interleaves_owners(world):
+    n = workloads.numels(workloads.qwen3_8b())
+    p = layout.plan(n, [HA_BF16] * len(n), world)
+    (cls,) = p.classes
+    for rank in range(world):
+        order = layout.push_chunk_order(cls, p.owner, rank, world, n, 16384)
+        natural = layout.chunk_table([n[i] for i in cls.indices], 16384)
+        assert sorted(map(tuple, order.tolist())) == sorted(map(tuple, natural.tolist()))
+        owners = [p.owner[cls.indices[int(t)]] for t in order["tensor"][:4 * world]]
+        # the first rounds visit every owner, starting after this rank and ending with it
+        assert owners[:world] == [(rank + d) % world for d in range(1, world + 1)]
+        assert len(set(owners)) == world
+
+
+def test_push_destinations_land_in_the_senders_region():
+    n = [1000, 64, 5000, 3, 70000]
+    p = layout.plan(n, [HA_BF16] * len(n), 3)
+    (cls,) = p.classes
+    bases = [1 << 40, 2 << 40, 3 << 40]
+    for rank in range(3):
+        dst = layout.push_destinations(cls, p.owner, rank, 2, bases, 0)
+        for k, i in enumerate(cls.indices):
+            o = p.owner[i]
+            elem = (dst[k] - bases[o]) // 2
+            assert elem == rank * cls.seg_len + cls.offset[i]
+            assert elem + n[i] <= (rank + 1) * cls.seg_len
+    assert layout.peer_deltas([100, 300, 700], 1) == [-200, 400]

@@ -1,7 +1,10 @@
-"""The optimizer at world size 2 on two GPUs over NCCL (skipped with fewer GPUs).
+"""The optimizer at world size 2 on two GPUs (skipped with fewer GPUs), in both
+communication modes: p2p (gradients pushed into the owners' buffers over NVLink, summed by
+the owner; parameters stored into every peer by the update kernel) and nccl (local pack,
+NCCL reduce-scatter and all-gather).
 
 Each rank runs tests/world_worker.py under torchrun on a world-size-2 golden case.  At
-world size 2 the reduce-scatter's sums have one rounding whatever the algorithm, so the
+world size 2 every reduction's sums have one rounding whatever the algorithm, so the
 owners' reduced gradients, norms and states can be held bit for bit to the oracle (torch-
 CUDA form, replaying this run's norms) and to the reference's own gloo run within the
 parity criterion.  The parameters must agree bit for bit across ranks.
@@ -28,9 +31,10 @@ def _gpus() -> int:
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("mode", ["p2p", "nccl"])
 @pytest.mark.parametrize("name", ["bf16_world2", "fp32_world2"])
-def test_world2_nccl_matches_oracle_and_reference(name, tmp_path):
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+def test_world2_matches_oracle_and_reference(name, mode, tmp_path):
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", HYBRIDAGENT_B200_COMM=mode)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29731",
            os.path.join(HERE, "world_worker.py"), name, str(tmp_path)]
@@ -39,6 +43,7 @@ def test_world2_nccl_matches_oracle_and_reference(name, tmp_path):
     res = [pickle.load(open(tmp_path / f"rank{r}.pkl", "rb")) for r in range(2)]
     case = CASES_BY_NAME[name]
     g = golden(name)
+    assert res[0]["mode"] == res[1]["mode"] == mode
     assert res[0]["norms"] == res[1]["norms"]
     assert res[0]["owner"] == g["owner"].tolist()
     for s, (mine, ref) in enumerate(zip(res[0]["norms"], g["norms"].tolist())):

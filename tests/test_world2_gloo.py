@@ -162,3 +162,144 @@ def test_world2_host_path_matches_reference(name):
         assert_state_close(master, g[f"master_{i}"], f"master[{i}]")
         if case.dtype == Z.BF16:
             assert_bits_equal(Z.narrow(master, Z.BF16), a, f"param[{i}]")
+
+
+def _rank_main_p2p(rank, world, port, name, queue):
+    """The p2p data flow: each rank pushes every gradient to the address
+    layout.push_destinations gives (in the owner's receive buffer, region <rank>), the owner
+    adds the regions in rank order and clips / updates its slots, and each new parameter is
+    stored at layout.peer_deltas offsets into every peer's packed parameters.  Device
+    memories are simulated as numpy arrays at fake base addresses; the stores that cross
+    ranks travel through gloo."""
+    import sys
+    sys.path[:0] = [os.path.dirname(os.path.dirname(os.path.abspath(__file__))), os.path.dirname(__file__),
+                    os.path.join(os.path.dirname(__file__), "golden")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch
+    import torch.distributed as dist
+
+    from cases import CASES_BY_NAME as C
+    from hybridagent_b200 import layout
+    from hybridagent_b200._lib import HA_BF16, HA_F32
+    from oracle import zero1 as Z
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        case = C[name]
+        code = HA_BF16 if case.dtype == Z.BF16 else HA_F32
+        numels = case.numels
+        plan = layout.plan(numels, [code] * len(numels), world)
+        (cls,) = plan.classes
+        seg = cls.seg_len
+        npdt = np.uint16 if case.dtype == Z.BF16 else np.float32
+        esz = np.dtype(npdt).itemsize
+        SPACE = 1 << 40
+        grad_bases = [(r + 1) * SPACE for r in range(world)]            # each rank's receive buffer
+        param_bases = [(r + 1) * SPACE + SPACE // 2 for r in range(world)]  # each rank's packed params
+        dst = layout.push_destinations(cls, plan.owner, rank, esz, grad_bases, 0)
+        deltas = layout.peer_deltas(param_bases, rank)
+        peers = [r for r in range(world) if r != rank]
+
+        def exchange(images):
+            """images[r]: this rank's stores into rank r's memory (NaN / sentinel = untouched)."""
+            everyone = [None] * world
+            dist.all_gather_object(everyone, images)
+            return [everyone[s][rank] for s in range(world)]
+
+        params = np.zeros(world * seg, npdt)
+        init = case.initial_params()
+        for i in cls.indices:
+            start = plan.owner[i] * seg + cls.offset[i]
+            params[start:start + numels[i]] = init[i]
+        owned = cls.owned(plan.owner, rank)
+        state = {i: [Z.widen(init[i], case.dtype).copy(), np.zeros(numels[i], np.float32),
+                     np.zeros(numels[i], np.float32), 0] for i in owned}
+        recv = np.zeros(world * seg, npdt)
+        norms = []
+        for s in range(case.steps):
+            grads = case.grads(s, rank)
+            used = torch.tensor([g is not None for g in grads], dtype=torch.uint8)
+            dist.all_reduce(used, op=dist.ReduceOp.MAX)
+            # push: write each gradient (zeros when absent) at its destination address
+            images = [dict() for _ in range(world)]
+            for k, i in enumerate(cls.indices):
+                owner = plan.owner[i]
+                elem = (dst[k] - grad_bases[owner]) // esz
+                assert rank * seg <= elem and elem + numels[i] <= (rank + 1) * seg  # region <rank> of the owner
+                g = grads[i] if grads[i] is not None and used[i] else np.zeros(numels[i], npdt)
+                images[owner][elem] = g
+            for img in exchange(images):
+                for elem, g in img.items():
+                    recv[elem:elem + len(g)] = g
+            # owner: add the regions in rank order, round once, square sums of the result
+            acc = Z.widen(recv[0:seg].copy(), case.dtype)
+            for r in range(1, world):
+                acc = acc + Z.widen(recv[r * seg:(r + 1) * seg], case.dtype)
+            own = Z.narrow(acc, case.dtype) if case.dtype != Z.F32 else acc.astype(np.float32)
+            recv[rank * seg:(rank + 1) * seg] = own
+            mine = {i: own[cls.offset[i]:cls.offset[i] + numels[i]].copy() for i in owned if used[i]}
+            total = torch.tensor([sum(Z.sumsq(g, case.dtype) for g in mine.values())], dtype=torch.float64)
+            dist.all_reduce(total)
+            norm = Z.norm_from_sumsq(float(total))
+            norms.append(norm)
+            scale = Z.clip_scale_for(norm, case.max_norm)
+            images = [dict() for _ in range(world)]
+            for i, g in mine.items():
+                st = state[i]
+                st[3] += 1
+                start = rank * seg + cls.offset[i]
+                p = None if case.dtype == Z.F32 else params[start:start + numels[i]].copy()
+                Z.adamw_tensor(Z.FORM_TORCH_CUDA, g, case.dtype, st[0], st[1], st[2], p, case.dtype, lr=case.lr,
+                               beta1=case.betas[0], beta2=case.betas[1], eps=case.eps,
+                               weight_decay=case.weight_decay, step=st[3], clip_scale=scale)
+                new = st[0] if p is None else p
+                params[start:start + numels[i]] = new
+                local_addr = param_bases[rank] + start * esz
+                for q, d in zip(peers, deltas):  # the fused all-gather: same element on every peer
+                    elem = (local_addr + d - param_bases[q]) // esz
+                    assert elem == start
+                    images[q][elem] = new.copy()
+            for img in exchange(images):
+                for elem, v in img.items():
+                    params[elem:elem + len(v)] = v
+        final = {i: params[plan.owner[i] * seg + cls.offset[i]:plan.owner[i] * seg + cls.offset[i] + numels[i]]
+                 for i in cls.indices}
+        queue.put((rank, norms, final, {i: tuple(st) for i, st in state.items()}, plan.owner))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("name", ["bf16_world2"])
+def test_world2_p2p_host_path_matches_reference(name):
+    import torch.multiprocessing as mp
+
+    from helpers import Z, assert_bits_equal, assert_state_close, golden
+
+    case = CASES_BY_NAME[name]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main_p2p, args=(r, 2, port, name, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in procs:
+        rank, norms, final, state, owner = q.get(timeout=300)
+        results[rank] = (norms, final, state, owner)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    g = golden(name)
+    assert results[0][0] == results[1][0]
+    for s, (mine, ref) in enumerate(zip(results[0][0], g["norms"].tolist())):
+        assert Z.isclose_norm(mine, ref, 1e-6), (s, mine, ref)
+    for i in range(len(case.shapes)):
+        a, b = results[0][1][i], results[1][1][i]
+        assert np.array_equal(a.view(np.uint8), b.view(np.uint8)), f"ranks disagree on param {i}"
+        owner = int(g["owner"][i])
+        master, m, v, steps = results[owner][2][i]
+        assert steps == int(g[f"param_steps_{i}"])
+        assert_bits_equal(m, g[f"exp_avg_{i}"], f"exp_avg[{i}]")
+        assert_state_close(v, g[f"exp_avg_sq_{i}"], f"exp_avg_sq[{i}]", max_ulp=3)
+        assert_state_close(master, g[f"master_{i}"], f"master[{i}]")
+        assert_bits_equal(Z.narrow(master, Z.BF16), a, f"param[{i}]")

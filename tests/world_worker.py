@@ -53,7 +53,7 @@ def main(name: str, out_dir: str) -> None:
             opt.step()
     torch.cuda.synchronize()
     result = {
-        "rank": rank, "norms": norms, "owner": opt.owner,
+        "rank": rank, "norms": norms, "owner": opt.owner, "mode": opt.comm_mode,
         "params": [to_numpy(p.data, case.dtype) for p in params],
         "state": {i: (to_numpy(opt.master[i], 0), to_numpy(opt.exp_avg[i], 0), to_numpy(opt.exp_avg_sq[i], 0),
                       opt.param_steps[i]) for i in opt.param_steps},
