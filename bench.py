@@ -45,6 +45,7 @@ sys.path.insert(0, ROOT)
 ALGO_BYTES_ADAMW = {"bf16": 28, "f16": 28, "f32": 28}   # per owned parameter, per AdamW launch
 ALGO_BYTES_SUMSQ = {"bf16": 2, "f16": 2, "f32": 4}
 FALLBACK_HBM_GBS = 6650.0
+NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's B200s (the NVLink roofline reference)
 TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "adamw_kernel_qwen3_8b.md")
 
 
@@ -342,6 +343,23 @@ def run_ours(args) -> None:
     algo = ALGO_BYTES_ADAMW["bf16"] * owned_params
     achieved = algo / (adamw_ms * 1e-3) / 1e9 if adamw_ms else None
     tpp = profiled_traffic_per_param()
+    nvlink = None
+    if world > 1 and opt.comm_mode == "p2p":
+        # fused compute + collective kernels: target time = max(HBM bytes / HBM peak, NVLink bytes / link)
+        foreign = n_params - owned_params  # gradients this rank sends, parameters it receives
+        push_link = 2 * foreign
+        adamw_link = 2 * owned_params * (world - 1)
+        nvlink = {}
+        for name, link_bytes, hbm_bytes in (("push", push_link, 4 * n_params),
+                                            ("adamw", adamw_link, algo + 2 * foreign)):
+            ms_phase = phases.get(name)
+            if not ms_phase:
+                continue
+            target = max(hbm_bytes / (peak * 1e9), link_bytes / (NVLINK_GBS * 1e9)) * 1e3
+            nvlink[name] = {"measured_ms": round(ms_phase, 3), "target_ms": round(target, 3),
+                            "frac": round(target / ms_phase, 4), "nvlink_bytes": link_bytes, "hbm_bytes": hbm_bytes,
+                            "link_gbs_achieved": round(link_bytes / (ms_phase * 1e-3) / 1e9, 1)}
+        nvlink["link_peak"] = f"{NVLINK_GBS} GB/s per direction (measured peer copy)"
     out = {
         "metric": "ZeRO-1 AdamW step Gparams/s",
         "value": round(n_params / (ms_max * 1e-3) / 1e9, 3),
@@ -370,6 +388,8 @@ def run_ours(args) -> None:
                      "traffic_source": None if tpp is None else "ncu dram__bytes_read+write per launch, "
                      "profiles/adamw_kernel_qwen3_8b.md, scaled to this launch's parameters"},
         "phases_ms": {k: round(v, 4) for k, v in phases.items()},
+        "comm_mode": opt.comm_mode,
+        "roofline_fused": nvlink,
         "last_norm": norm,
         "cpu_baseline": cpu,
         "e2e": e2e,
