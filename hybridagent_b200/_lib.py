@@ -78,6 +78,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "ha_comm_unique_id": ([_vp], ctypes.c_int),
     "ha_comm_init": ([_vp, _i32, _i32, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "ha_comm_destroy": ([_vp], ctypes.c_int),
+    "ha_comm_abort": ([_vp], ctypes.c_int),
     "ha_reduce_scatter": ([_vp, _vp, _vp, _sz, ctypes.c_int, _vp], ctypes.c_int),
     "ha_all_gather": ([_vp, _vp, _vp, _sz, ctypes.c_int, _vp], ctypes.c_int),
     "ha_all_reduce_sum": ([_vp, _vp, _sz, ctypes.c_int, _vp], ctypes.c_int),

@@ -28,6 +28,7 @@ struct Nccl {
   decltype(&ncclGetUniqueId) GetUniqueId;
   decltype(&ncclCommInitRank) CommInitRank;
   decltype(&ncclCommDestroy) CommDestroy;
+  decltype(&ncclCommAbort) CommAbort;
   decltype(&ncclReduceScatter) ReduceScatter;
   decltype(&ncclAllGather) AllGather;
   decltype(&ncclAllReduce) AllReduce;
@@ -53,7 +54,8 @@ void load_nccl() {
     return;
   }
   bool ok = bind(h, "ncclGetUniqueId", &g_nccl.GetUniqueId) && bind(h, "ncclCommInitRank", &g_nccl.CommInitRank) &&
-            bind(h, "ncclCommDestroy", &g_nccl.CommDestroy) && bind(h, "ncclReduceScatter", &g_nccl.ReduceScatter) &&
+            bind(h, "ncclCommDestroy", &g_nccl.CommDestroy) && bind(h, "ncclCommAbort", &g_nccl.CommAbort) &&
+            bind(h, "ncclReduceScatter", &g_nccl.ReduceScatter) &&
             bind(h, "ncclAllGather", &g_nccl.AllGather) && bind(h, "ncclAllReduce", &g_nccl.AllReduce) &&
             bind(h, "ncclGetErrorString", &g_nccl.GetErrorString);
   if (!ok) g_nccl_error = "libnccl.so.2 lacks an expected symbol";
@@ -89,6 +91,7 @@ struct ha_comm {
   ncclComm_t comm;
   int world;
   int rank;
+  bool aborted;
 };
 
 extern "C" int ha_comm_unique_id(uint8_t out[128]) {
@@ -108,42 +111,62 @@ extern "C" int ha_comm_init(const uint8_t id[128], int32_t world, int32_t rank, 
   std::memcpy(uid.internal, id, 128);
   ncclComm_t c = nullptr;
   if (int rc = nccl_status(g_nccl.CommInitRank(&c, world, uid, rank), "ncclCommInitRank")) return rc;
-  *out = new ha_comm{c, world, rank};
+  *out = new ha_comm{c, world, rank, false};
   return HA_OK;
 }
 
 extern "C" int ha_comm_destroy(ha_comm* comm) {
   if (comm == nullptr) return HA_OK;
   int rc = HA_OK;
-  if (g_nccl.ok && comm->comm != nullptr) rc = nccl_status(g_nccl.CommDestroy(comm->comm), "ncclCommDestroy");
+  if (g_nccl.ok && comm->comm != nullptr && !comm->aborted)
+    rc = nccl_status(g_nccl.CommDestroy(comm->comm), "ncclCommDestroy");
   delete comm;
   return rc;
 }
 
+extern "C" int ha_comm_abort(ha_comm* comm) {
+  if (comm == nullptr) return ha::fail(HA_ERR_INVALID, "ha_comm_abort: NULL");
+  if (comm->aborted || comm->comm == nullptr || !g_nccl.ok) return HA_OK;
+  comm->aborted = true;
+  return nccl_status(g_nccl.CommAbort(comm->comm), "ncclCommAbort");
+}
+
+namespace {
+int usable(ha_comm* comm, const char* what) {
+  if (comm == nullptr) return ha::fail(HA_ERR_INVALID, "%s: NULL communicator", what);
+  if (comm->aborted) return ha::fail(HA_ERR_NCCL, "%s: communicator was aborted", what);
+  return HA_OK;
+}
+}  // namespace
+
 extern "C" int ha_reduce_scatter(ha_comm* comm, const void* send, void* recv, size_t count, int dtype, void* stream) {
   ncclDataType_t t;
-  if (comm == nullptr || !nccl_type(dtype, &t)) return ha::fail(HA_ERR_INVALID, "ha_reduce_scatter: bad arguments");
+  if (int rc = usable(comm, "ha_reduce_scatter")) return rc;
+  if (!nccl_type(dtype, &t)) return ha::fail(HA_ERR_INVALID, "ha_reduce_scatter: bad arguments");
   return nccl_status(g_nccl.ReduceScatter(send, recv, count, t, ncclSum, comm->comm, static_cast<cudaStream_t>(stream)),
                      "ncclReduceScatter");
 }
 
 extern "C" int ha_all_gather(ha_comm* comm, const void* send, void* recv, size_t count, int dtype, void* stream) {
   ncclDataType_t t;
-  if (comm == nullptr || !nccl_type(dtype, &t)) return ha::fail(HA_ERR_INVALID, "ha_all_gather: bad arguments");
+  if (int rc = usable(comm, "ha_all_gather")) return rc;
+  if (!nccl_type(dtype, &t)) return ha::fail(HA_ERR_INVALID, "ha_all_gather: bad arguments");
   return nccl_status(g_nccl.AllGather(send, recv, count, t, comm->comm, static_cast<cudaStream_t>(stream)),
                      "ncclAllGather");
 }
 
 extern "C" int ha_all_reduce_sum(ha_comm* comm, void* buf, size_t count, int dtype, void* stream) {
   ncclDataType_t t;
-  if (comm == nullptr || !nccl_type(dtype, &t)) return ha::fail(HA_ERR_INVALID, "ha_all_reduce_sum: bad arguments");
+  if (int rc = usable(comm, "ha_all_reduce_sum")) return rc;
+  if (!nccl_type(dtype, &t)) return ha::fail(HA_ERR_INVALID, "ha_all_reduce_sum: bad arguments");
   return nccl_status(g_nccl.AllReduce(buf, buf, count, t, ncclSum, comm->comm, static_cast<cudaStream_t>(stream)),
                      "ncclAllReduce(sum)");
 }
 
 extern "C" int ha_all_reduce_max(ha_comm* comm, void* buf, size_t count, int dtype, void* stream) {
   ncclDataType_t t;
-  if (comm == nullptr || !nccl_type(dtype, &t)) return ha::fail(HA_ERR_INVALID, "ha_all_reduce_max: bad arguments");
+  if (int rc = usable(comm, "ha_all_reduce_max")) return rc;
+  if (!nccl_type(dtype, &t)) return ha::fail(HA_ERR_INVALID, "ha_all_reduce_max: bad arguments");
   return nccl_status(g_nccl.AllReduce(buf, buf, count, t, ncclMax, comm->comm, static_cast<cudaStream_t>(stream)),
                      "ncclAllReduce(max)");
 }

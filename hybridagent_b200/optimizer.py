@@ -240,8 +240,10 @@ class ZeroOneAdamW:
     """ZeRO-1 AdamW over CUDA parameters (drop-in for hybrid_rl.optimizer.ZeroOneAdamW)."""
 
     def __init__(self, param_groups, *, rank: int, world_size: int, betas=(0.9, 0.999), eps: float = 1e-8,
-                 weight_decay: float = 0.0, use_8bit: bool = False):
-        # argument handling and errors as optimizer.py:24-44
+                 weight_decay: float = 0.0, use_8bit: bool = False, comm_timeout_s: float | None = None):
+        # argument handling and errors as optimizer.py:24-44; comm_timeout_s (world > 1): seconds a
+        # collective may wait for the other ranks before the communicator is aborted and the call
+        # raises CommFailure (default HYBRIDAGENT_B200_COMM_TIMEOUT_S or 1800)
         self.rank = int(rank)
         self.world = int(world_size)
         self.betas = tuple(float(value) for value in betas)
@@ -295,11 +297,14 @@ class ZeroOneAdamW:
             self.comm_mode = "local"
             if self.world > 1:
                 from .comm import NcclComm
-                self._comm = NcclComm(self.rank, self.world)
+                self._comm = NcclComm(self.rank, self.world, timeout_s=comm_timeout_s)
             self._classes = [_Class(self, c) for c in self._plan.classes]
             self._norm_buf = torch.zeros(len(self._classes), dtype=torch.float64, device=self.device)
             self._used_dev = torch.zeros(len(self.params), dtype=torch.uint8, device=self.device)
             self._barrier_buf = torch.zeros(1, dtype=torch.int32, device=self.device)
+            if self.world > 1:  # pinned landing buffers of the host reads (CommFailure-aware waits)
+                self._used_host = torch.zeros(len(self.params), dtype=torch.uint8, pin_memory=True)
+                self._norm_host = torch.zeros(len(self._classes), dtype=torch.float64, pin_memory=True)
             if self.world > 1:
                 self._setup_world()
             torch.cuda.current_stream().synchronize()
@@ -328,7 +333,8 @@ class ZeroOneAdamW:
             ok = 1 if self._peer_map.ok else 0
         flag = torch.tensor([1 - ok], dtype=torch.int32, device=self.device)
         self._comm.all_reduce_max(flag, HA_I32)  # every rank takes the same mode
-        use_p2p = int(flag.item()) == 0
+        use_p2p = int(self._comm.read(flag, torch.zeros(1, dtype=torch.int32, pin_memory=True),
+                                      "all-reduce(max) of the p2p flag")[0]) == 0
         if not use_p2p and self._peer_map is not None:
             self._peer_map.close()
             self._peer_map = None
@@ -406,7 +412,9 @@ class ZeroOneAdamW:
             local = np.fromiter((p.grad is not None for p in self.params), dtype=np.uint8, count=len(self.params))
             self._used_dev.copy_(torch.from_numpy(local), non_blocking=False)
             self._comm.all_reduce_max(self._used_dev, HA_U8)
-            used = self._used_dev.cpu().numpy().astype(bool)
+            # a rank that stopped answering ends here (CommFailure), before any peer store
+            used = self._comm.read(self._used_dev, self._used_host, "all-reduce(max) of the used mask")
+            used = used.numpy().astype(bool)
             keep = []  # gradients that must stay alive until the move kernel has read them
             for c in self._classes:
                 cp = c.move.np
@@ -488,7 +496,9 @@ class ZeroOneAdamW:
                 self._phase("sumsq", False)
             if self.world > 1:
                 self._comm.all_reduce_sum(self._norm_buf, HA_F64)
-            partial = self._norm_buf.cpu().tolist()
+                partial = self._comm.read(self._norm_buf, self._norm_host, "all-reduce(sum) of the norm").tolist()
+            else:
+                partial = self._norm_buf.cpu().tolist()
         total = np.float32(sum(partial))  # the reference's total is an fp32 tensor
         norm = float(np.sqrt(total))      # float(total.sqrt()), optimizer.py:154
         if max_norm > 0 and norm > max_norm:

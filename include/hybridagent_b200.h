@@ -218,6 +218,11 @@ int ha_comm_unique_id(uint8_t out[128]);
 /* Communicator on the calling thread's current CUDA device. */
 int ha_comm_init(const uint8_t id[128], int32_t world, int32_t rank, ha_comm** out);
 int ha_comm_destroy(ha_comm* comm);
+/* Aborts the communicator (ncclCommAbort): collectives blocked on a rank that stopped
+ * answering end, and every later call on it returns HA_ERR_NCCL.  Safe from a watchdog
+ * thread while the caller waits on the stream; the caller must not enqueue concurrently.
+ * The reference relies on the process group's timeout for this (hybrid_rl/dist.py:29). */
+int ha_comm_abort(ha_comm* comm);
 
 /* SUM reduce-scatter: recv[count] = sum over ranks of send[rank*count .. +count]
  * (replaces the per-owner bucketed dist.reduce of optimizer.py:108-142). In place when

@@ -133,6 +133,9 @@ CASES = [
     Case("bf16_world2", 10, _SMALL, BF16, steps=3, world=2, grad_sigma=1e-2,
          overrides={(0, 1, 3): "none", (1, 0, 4): "none", (1, -1, 9): "none", (2, 0, 0): "zero"}),
     Case("fp32_world2", 11, _SMALL, F32, steps=3, world=2, grad_sigma=1e-2, preload_state=True),
+    # rank 1 alone holds a +inf at step 1: every rank must see a non-finite norm and skip
+    Case("bf16_world2_inf", 12, _SMALL, BF16, steps=3, world=2, grad_sigma=1e-2, overrides={(1, 1, 5): "inf"},
+         call_step_after_nonfinite=False),
 ]
 
 CASES_BY_NAME = {c.name: c for c in CASES}

@@ -32,7 +32,7 @@ def _gpus() -> int:
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("mode", ["p2p", "nccl"])
-@pytest.mark.parametrize("name", ["bf16_world2", "fp32_world2"])
+@pytest.mark.parametrize("name", ["bf16_world2", "fp32_world2", "bf16_world2_inf"])
 def test_world2_matches_oracle_and_reference(name, mode, tmp_path):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", HYBRIDAGENT_B200_COMM=mode)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
@@ -63,3 +63,25 @@ def test_world2_matches_oracle_and_reference(name, mode, tmp_path):
         # after all_reduce_grads only the owner holds a gradient
         other = 1 - owner
         assert res[other]["grads"][-1][i] is None
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+def test_stalled_peer_raises_comm_failure(tmp_path):
+    """Rank 1 stalls on the host between steps (12 s) while rank 0's next collective waits:
+    the communicator watchdog (5 s timeout) aborts it and the step raises CommFailure on
+    rank 0 instead of hanging; rank 1 learns of it on the host before its next launch.  The
+    failure is injected on the host only; no rank dies with memory mapped by another."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "20", "150", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29733",
+           os.path.join(HERE, "world_worker.py"), "peer_delay", str(tmp_path)]
+    proc = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    logs = "".join(f"--- rank{r}.log\n" + (tmp_path / f"rank{r}.log").read_text()
+                   for r in range(2) if (tmp_path / f"rank{r}.log").exists())
+    assert proc.returncode == 0, logs + proc.stdout[-4000:] + proc.stderr[-6000:]
+    r0 = pickle.load(open(tmp_path / "rank0.pkl", "rb"))
+    r1 = pickle.load(open(tmp_path / "rank1.pkl", "rb"))
+    assert r0["mode"] == r1["mode"] == "p2p"
+    assert r0["error"] is not None and "did not complete within 5 s" in r0["error"], logs
+    assert 5.0 <= r0["elapsed"] < 60.0, logs
+    assert r1["error"] == "peer reported CommFailure before this rank's next launch", logs

@@ -13,6 +13,86 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path[:0] = [os.path.dirname(HERE), HERE, os.path.join(HERE, "golden")]
 
 
+def peer_delay(out_dir: str) -> None:
+    """Both ranks take one step; then rank 1 stalls on the host (a 12 s sleep, nothing of
+    its in flight) while rank 0 starts the next step.  Rank 0's first collective must end
+    in CommFailure after the 5 s watchdog timeout, before any of its kernels reads or
+    writes rank 1's memory; rank 1, resuming, learns of the failure on the host (rank 0's
+    result file) and launches nothing.  Progress lines and periodic stack dumps go to files
+    for diagnosis."""
+    import faulthandler
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from cases import CASES_BY_NAME
+    from helpers import to_torch
+    from hybridagent_b200 import ZeroOneAdamW
+    from hybridagent_b200.comm import CommFailure
+
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    log = open(os.path.join(out_dir, f"rank{rank}.log"), "w", buffering=1)
+    faulthandler.dump_traceback_later(20, repeat=True, file=log)
+    t_start = time.monotonic()
+
+    def note(msg):
+        log.write(f"{time.monotonic() - t_start:8.3f} {msg}\n")
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    case = CASES_BY_NAME["bf16_world2"]
+    params = [torch.nn.Parameter(to_torch(p, case.dtype, s, dev)) for p, s in zip(case.initial_params(), case.shapes)]
+    opt = ZeroOneAdamW([{"params": params, "lr": case.lr}], rank=rank, world_size=world, comm_timeout_s=5.0)
+    note(f"built, mode {opt.comm_mode}")
+
+    def step(s):
+        opt.zero_grad(set_to_none=True)
+        for p, g, shape in zip(params, case.grads(s, rank), case.shapes):
+            p.grad = None if g is None else to_torch(g, case.dtype, shape, dev)
+        note(f"step {s}: all_reduce_grads")
+        opt.all_reduce_grads()
+        note(f"step {s}: clip_grad_norm")
+        opt.clip_grad_norm(case.max_norm)
+        note(f"step {s}: step")
+        opt.step()
+
+    step(0)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    note("step 0 done on both ranks")
+    result = {"rank": rank, "mode": opt.comm_mode}
+    if rank == 1:
+        time.sleep(12.0)  # host-injected stall, nothing in flight
+        note("resuming after the stall")
+        if os.path.exists(os.path.join(out_dir, "rank0.pkl")):
+            # rank 0 already gave up on this exchange: learn it on the host and launch nothing
+            result["error"] = "peer reported CommFailure before this rank's next launch"
+            result["elapsed"] = 0.0
+            note(f"result {result}")
+            with open(os.path.join(out_dir, f"rank{rank}.pkl"), "wb") as f:
+                pickle.dump(result, f)
+            faulthandler.cancel_dump_traceback_later()
+            log.close()
+            os._exit(0)
+    t0 = time.monotonic()
+    try:
+        step(1)
+        torch.cuda.synchronize()
+        result["error"] = None
+    except CommFailure as e:
+        result["error"] = str(e)
+    result["elapsed"] = time.monotonic() - t0
+    note(f"result {result}")
+    with open(os.path.join(out_dir, f"rank{rank}.pkl"), "wb") as f:
+        pickle.dump(result, f)
+    faulthandler.cancel_dump_traceback_later()
+    log.close()
+    os._exit(0)  # the communicator is aborted: skip collective teardown
+
+
 def main(name: str, out_dir: str) -> None:
     import torch
     import torch.distributed as dist
@@ -67,4 +147,7 @@ def main(name: str, out_dir: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1], sys.argv[2])
+    if sys.argv[1] == "peer_delay":
+        peer_delay(sys.argv[2])
+    else:
+        main(sys.argv[1], sys.argv[2])
