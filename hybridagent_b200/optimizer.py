@@ -302,14 +302,16 @@ class ZeroOneAdamW:
             self._norm_buf = torch.zeros(len(self._classes), dtype=torch.float64, device=self.device)
             self._used_dev = torch.zeros(len(self.params), dtype=torch.uint8, device=self.device)
             self._barrier_buf = torch.zeros(1, dtype=torch.int32, device=self.device)
-            if self.world > 1:  # pinned landing buffers of the host reads (CommFailure-aware waits)
+            # pinned landing buffers of the host reads (deadline-aware waits at world > 1)
+            self._norm_host = torch.zeros(len(self._classes), dtype=torch.float64, pin_memory=True)
+            if self.world > 1:
                 self._used_host = torch.zeros(len(self.params), dtype=torch.uint8, pin_memory=True)
-                self._norm_host = torch.zeros(len(self._classes), dtype=torch.float64, pin_memory=True)
             if self.world > 1:
                 self._setup_world()
             torch.cuda.current_stream().synchronize()
         self._pending_clip: float | None = None
         self._fused_sumsq: list | None = None
+        self._grad_cache: dict[int, tuple] = {}
         self.timer = None  # optional phase timer: .begin(name) / .end(name) around kernel launches
         self.launches = 0  # kernels of libhybridagent_b200 launched so far
 
@@ -374,6 +376,18 @@ class ZeroOneAdamW:
             grads.append(g)
         return grads, ptrs
 
+    def _cached_grads(self, k: int, c: _Class) -> tuple[list[torch.Tensor | None], np.ndarray]:
+        """_owned_grads, reusing the pointers found by the previous call of this step (the
+        gradient objects are checked by identity, which costs far less than re-reading them)."""
+        cached = self._grad_cache.get(k)
+        if cached is not None:
+            orig, grads, ptrs = cached
+            if all(self.params[i].grad is g for i, g in zip(c.owned, orig)):
+                return grads, ptrs
+        grads, ptrs = self._owned_grads(c)
+        self._grad_cache[k] = ([self.params[i].grad for i in c.owned], grads, ptrs)
+        return grads, ptrs
+
     def _upload_table(self, c: _Class, grad_ptrs: np.ndarray, advance: bool) -> None:
         tab = c.table.np[:len(c.owned)]
         tab["grad"] = grad_ptrs
@@ -394,6 +408,7 @@ class ZeroOneAdamW:
         """optimizer.py:88-93."""
         self._pending_clip = None
         self._fused_sumsq = None
+        self._grad_cache = {}
         for parameter in self.params:
             if set_to_none:
                 parameter.grad = None
@@ -460,6 +475,7 @@ class ZeroOneAdamW:
                     self._comm.reduce_scatter(c.packed_grad.data_ptr(), own, c.layout.seg_len, c.code)
                 self._phase("reduce_scatter", False)
             del keep
+            self._grad_cache = {}
             for c in self._classes:
                 for i in c.layout.indices:
                     if used[i] and self.owner[i] == self.rank:
@@ -482,8 +498,8 @@ class ZeroOneAdamW:
                 self.params[i].grad is g for g, i in zip(fused, (i for c in self._classes for i in c.owned)))
             if not reuse:
                 keep = []  # contiguous copies of strided gradients must outlive the launches
-                for c in self._classes:
-                    grads, ptrs = self._owned_grads(c)
+                for k, c in enumerate(self._classes):
+                    grads, ptrs = self._cached_grads(k, c)
                     keep.append(grads)
                     self._upload_table(c, ptrs, advance=False)
                 self._phase("sumsq", True)
@@ -498,7 +514,11 @@ class ZeroOneAdamW:
                 self._comm.all_reduce_sum(self._norm_buf, HA_F64)
                 partial = self._comm.read(self._norm_buf, self._norm_host, "all-reduce(sum) of the norm").tolist()
             else:
-                partial = self._norm_buf.cpu().tolist()
+                self._norm_host.copy_(self._norm_buf, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record()
+                ev.synchronize()
+                partial = self._norm_host.tolist()
         total = np.float32(sum(partial))  # the reference's total is an fp32 tensor
         norm = float(np.sqrt(total))      # float(total.sqrt()), optimizer.py:154
         if max_norm > 0 and norm > max_norm:
@@ -513,6 +533,7 @@ class ZeroOneAdamW:
             return
         scale, self._pending_clip = self._pending_clip, None
         self._fused_sumsq = None  # the gradients change below
+        self._grad_cache = {}
         with torch.cuda.device(self.device):
             keep = []
             for c in self._classes:
@@ -527,6 +548,9 @@ class ZeroOneAdamW:
                     _lib.call("ha_scale_grads", c.table.ptr, chunks.data_ptr(), n, HA_ADAMW_CHUNK, c.code,
                               sc.clip_mult, self._stream())
                     self.launches += 1
+                for i, g in zip(c.owned, grads):  # strided gradients were scaled in a contiguous copy
+                    if g is not None and g is not self.params[i].grad:
+                        self.params[i].grad.copy_(g)
 
     @torch.no_grad()
     def step(self) -> None:
@@ -536,8 +560,8 @@ class ZeroOneAdamW:
         scale, self._pending_clip = self._pending_clip, None
         with torch.cuda.device(self.device):
             launches, keep = [], []
-            for c in self._classes:
-                grads, ptrs = self._owned_grads(c)
+            for k, c in enumerate(self._classes):
+                grads, ptrs = self._cached_grads(k, c)
                 keep.append(grads)
                 self._upload_table(c, ptrs, advance=True)
                 sc = _lib.AdamwScalars()

@@ -182,3 +182,21 @@ def test_mixed_dtypes_and_strided_grads():
         assert_bits_equal(to_numpy(opt.exp_avg[i], 0), m, f"exp_avg[{i}]")
         assert_bits_equal(to_numpy(opt.exp_avg_sq[i], 0), v, f"exp_avg_sq[{i}]")
         assert_bits_equal(to_numpy(params[i].data, d), ora.params[i], f"param[{i}]")
+
+
+def test_apply_pending_clip_scales_strided_gradients_in_place():
+    import torch
+    from hybridagent_b200 import ZeroOneAdamW
+    rng = np.random.default_rng(8)
+    shape = (48, 80)
+    g = Z.to_bf16((rng.standard_normal(48 * 80) * 0.5).astype(np.float32))
+    p = torch.nn.Parameter(torch.zeros(shape, dtype=torch.bfloat16, device="cuda"))
+    opt = ZeroOneAdamW([{"params": [p], "lr": 1e-3}], rank=0, world_size=1)
+    p.grad = to_torch(g, Z.BF16, shape, "cuda").t().contiguous().t()
+    assert not p.grad.is_contiguous()
+    n = opt.clip_grad_norm(1.0)
+    assert n > 1.0
+    opt.apply_pending_clip()
+    want = g.copy()
+    Z.clip_inplace(want, Z.BF16, Z.FORM_TORCH_CUDA, 1.0 / (n + 1e-6))
+    assert_bits_equal(to_numpy(p.grad, Z.BF16), want, "strided clipped grad")
