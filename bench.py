@@ -139,8 +139,10 @@ class PhaseTimer:
             e.record()
             self.pairs.setdefault(name, []).append((self._open.pop(name), e))
 
-    def mean_ms(self) -> dict[str, float]:
-        return {k: sum(a.elapsed_time(b) for a, b in v) / len(v) for k, v in self.pairs.items()}
+    def per_step_ms(self, steps: int) -> dict[str, float]:
+        """Total time of each phase over the timed region divided by the steps (phases that
+        run several times a step, like the exchange rounds, add up)."""
+        return {k: sum(a.elapsed_time(b) for a, b in v) / steps for k, v in self.pairs.items()}
 
 
 class ClockSampler:
@@ -291,7 +293,7 @@ def run_ours(args) -> None:
         timer.enabled = False
     launches = opt.launches - launches0
     ms = start.elapsed_time(stop) / args.steps
-    phases = timer.mean_ms()
+    phases = timer.per_step_ms(args.steps)
     t = torch.tensor([ms, phases.get("adamw", 0.0)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

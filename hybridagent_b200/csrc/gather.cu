@@ -1,8 +1,10 @@
 // Multi-tensor copy / zero-fill (sm_100a).
 //
-// Packs every rank's gradients into the owner-major reduce-scatter buffer in one launch,
-// replacing the per-tensor `flat[offset:offset+n].copy_(grad)` / `.zero_()` bucket
-// packing of hybrid_rl/optimizer.py:126-135.  One CTA copies one chunk of one table
+// Moves every rank's gradients in one launch, replacing the per-tensor
+// `flat[offset:offset+n].copy_(grad)` / `.zero_()` bucket packing of
+// hybrid_rl/optimizer.py:126-135: into the local owner-major pack (nccl mode) or, with
+// peer-mapped destinations, straight into the owners' receive windows (p2p mode).  Stream
+// order makes the stores visible to the collective enqueued after the launch.  One CTA copies one chunk of one table
 // entry with 16-byte loads and stores when both ends are 16-byte aligned.
 #include <type_traits>
 
@@ -42,17 +44,13 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(const ha_copy* __restr
   }
 }
 
-}  // namespace
-}  // namespace ha
-
-extern "C" int ha_gather(const ha_copy* d_copies, const ha_chunk* d_chunks, int64_t n_chunks, int64_t chunk_elems,
-                         int elem_bytes, void* stream) {
-  using namespace ha;
-  if (elem_bytes != 2 && elem_bytes != 4) return fail(HA_ERR_UNSUPPORTED, "ha_gather: elem_bytes %d", elem_bytes);
-  if (chunk_elems <= 0 || chunk_elems % 8 != 0) return fail(HA_ERR_INVALID, "ha_gather: chunk_elems %lld", (long long)chunk_elems);
-  if (n_chunks < 0 || n_chunks > 0x7fffffffLL) return fail(HA_ERR_INVALID, "ha_gather: n_chunks %lld", (long long)n_chunks);
+int launch_gather(const ha_copy* d_copies, const ha_chunk* d_chunks, int64_t n_chunks, int64_t chunk_elems,
+                  int elem_bytes, void* stream, const char* what) {
+  if (elem_bytes != 2 && elem_bytes != 4) return fail(HA_ERR_UNSUPPORTED, "%s: elem_bytes %d", what, elem_bytes);
+  if (chunk_elems <= 0 || chunk_elems % 8 != 0) return fail(HA_ERR_INVALID, "%s: chunk_elems %lld", what, (long long)chunk_elems);
+  if (n_chunks < 0 || n_chunks > 0x7fffffffLL) return fail(HA_ERR_INVALID, "%s: n_chunks %lld", what, (long long)n_chunks);
   if (n_chunks == 0) return HA_OK;
-  if (d_copies == nullptr || d_chunks == nullptr) return fail(HA_ERR_INVALID, "ha_gather: NULL table");
+  if (d_copies == nullptr || d_chunks == nullptr) return fail(HA_ERR_INVALID, "%s: NULL table", what);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid(static_cast<unsigned>(n_chunks));
   if (elem_bytes == 2) {
@@ -60,5 +58,13 @@ extern "C" int ha_gather(const ha_copy* d_copies, const ha_chunk* d_chunks, int6
   } else {
     gather_kernel<4><<<grid, kThreads, 0, st>>>(d_copies, d_chunks, chunk_elems);
   }
-  return check_launch("gather_kernel");
+  return check_launch(what);
+}
+
+}  // namespace
+}  // namespace ha
+
+extern "C" int ha_gather(const ha_copy* d_copies, const ha_chunk* d_chunks, int64_t n_chunks, int64_t chunk_elems,
+                         int elem_bytes, void* stream) {
+  return ha::launch_gather(d_copies, d_chunks, n_chunks, chunk_elems, elem_bytes, stream, "ha_gather");
 }

@@ -8,8 +8,8 @@
 //     owner's receive buffer (ha_gather with peer destinations) -- the pack and the
 //     transfer in one pass over the local gradients;
 //   * ha_sum_regions (this file): the owner adds the W regions in fp32 in rank order,
-//     rounds once to the gradient dtype, writes the sum over its own region and emits the
-//     sum of squares of the result (the global norm's partials) in the same pass;
+//     rounds once to the gradient dtype, writes the sum into its own gradient buffer and
+//     emits the sum of squares of the result (the global norm's partials) in the same pass;
 //   * ha_adamw_step_peers (adamw.cu): the update also stores each new parameter value
 //     into every peer's parameter buffer (the all-gather fused into the update).
 // Ordering between ranks comes from the caller's NCCL collectives between these launches
@@ -61,15 +61,15 @@ __device__ __forceinline__ void store4_as(void* base, int64_t e, float4 x) {
 }
 
 // regions: W consecutive regions of region_elems elements; the sum of elements [0, count)
-// of every region lands in region `rank`.
+// of every region lands in `out` (which may be one of the regions).
 template <int DT>
-__global__ void __launch_bounds__(kThreads) sum_regions_kernel(void* __restrict__ regions, int world, int rank,
-                                                               int64_t region_elems, int64_t count,
+__global__ void __launch_bounds__(kThreads) sum_regions_kernel(const void* regions, int world, int64_t region_elems,
+                                                               int64_t count, void* out,
                                                                double* __restrict__ partials) {
   __shared__ double red[kThreads / 32];
   using raw = typename Elem<DT>::raw;
-  raw* base = static_cast<raw*>(regions);
-  raw* own = base + int64_t(rank) * region_elems;
+  const raw* base = static_cast<const raw*>(regions);
+  raw* own = static_cast<raw*>(out);
   const int64_t begin = int64_t(blockIdx.x) * kChunk;
   const int64_t end = min(begin + kChunk, count);
   double acc = 0.0;
@@ -182,19 +182,19 @@ extern "C" int ha_ipc_close(void* ptr) {
   return ha::cuda_status(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
 }
 
-extern "C" int ha_sum_regions(void* d_regions, int32_t world, int32_t rank, int64_t region_elems, int64_t count,
-                              int dtype, double* d_partials, double* d_out, void* stream) {
+extern "C" int ha_sum_regions(const void* d_regions, int32_t world, int64_t region_elems, int64_t count,
+                              void* d_sum, int dtype, double* d_partials, double* d_out, void* stream) {
   using namespace ha;
   if (!valid_float_dtype(dtype)) return fail(HA_ERR_UNSUPPORTED, "ha_sum_regions: dtype %d", dtype);
-  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world)
-    return fail(HA_ERR_INVALID, "ha_sum_regions: world %d rank %d (at most %d ranks)", world, rank, kMaxWorld);
+  if (world < 1 || world > kMaxWorld)
+    return fail(HA_ERR_INVALID, "ha_sum_regions: world %d (at most %d ranks)", world, kMaxWorld);
   if (count < 0 || count > region_elems || region_elems % 64 != 0)
     return fail(HA_ERR_INVALID, "ha_sum_regions: count %lld, region %lld (multiple of 64 elements)",
                 (long long)count, (long long)region_elems);
-  if (d_out == nullptr || (count > 0 && (d_regions == nullptr || d_partials == nullptr)))
+  if (d_out == nullptr || (count > 0 && (d_regions == nullptr || d_partials == nullptr || d_sum == nullptr)))
     return fail(HA_ERR_INVALID, "ha_sum_regions: NULL buffer");
-  if ((reinterpret_cast<uintptr_t>(d_regions) & 15) != 0)
-    return fail(HA_ERR_INVALID, "ha_sum_regions: regions must be 16-byte aligned");
+  if (((reinterpret_cast<uintptr_t>(d_regions) | reinterpret_cast<uintptr_t>(d_sum)) & 15) != 0)
+    return fail(HA_ERR_INVALID, "ha_sum_regions: regions and sum must be 16-byte aligned");
   const int64_t n_chunks = (count + kChunk - 1) / kChunk;
   if (n_chunks > 0x7fffffffLL) return fail(HA_ERR_INVALID, "ha_sum_regions: too many chunks");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -202,13 +202,13 @@ extern "C" int ha_sum_regions(void* d_regions, int32_t world, int32_t rank, int6
     const dim3 grid(static_cast<unsigned>(n_chunks));
     switch (dtype) {
       case HA_F32:
-        sum_regions_kernel<HA_F32><<<grid, kThreads, 0, st>>>(d_regions, world, rank, region_elems, count, d_partials);
+        sum_regions_kernel<HA_F32><<<grid, kThreads, 0, st>>>(d_regions, world, region_elems, count, d_sum, d_partials);
         break;
       case HA_BF16:
-        sum_regions_kernel<HA_BF16><<<grid, kThreads, 0, st>>>(d_regions, world, rank, region_elems, count, d_partials);
+        sum_regions_kernel<HA_BF16><<<grid, kThreads, 0, st>>>(d_regions, world, region_elems, count, d_sum, d_partials);
         break;
       default:
-        sum_regions_kernel<HA_F16><<<grid, kThreads, 0, st>>>(d_regions, world, rank, region_elems, count, d_partials);
+        sum_regions_kernel<HA_F16><<<grid, kThreads, 0, st>>>(d_regions, world, region_elems, count, d_sum, d_partials);
         break;
     }
     if (int rc = check_launch("sum_regions_kernel")) return rc;

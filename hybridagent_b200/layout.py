@@ -121,6 +121,96 @@ def peer_deltas(param_bases: list[int], rank: int) -> list[int]:
     return [b - param_bases[rank] for r, b in enumerate(param_bases) if r != rank]
 
 
+@dataclass
+class Pieces:
+    """The parts of a dtype class's gradients that one exchange round moves.
+
+    Round k covers elements [k*S, (k+1)*S) of every owner's segment (S = round_elems), so a
+    tensor whose slot crosses a multiple of S is split.  Entry j: element ``src_off[j]`` of
+    table entry ``tensor[j]`` (an index into ``cls.indices``), ``count[j]`` elements, owned
+    by ``owner[j]``, landing at element ``dst_off[j]`` of the sender's region of that
+    round's receive window; ``round[j]`` is its round."""
+    tensor: np.ndarray
+    src_off: np.ndarray
+    owner: np.ndarray
+    dst_off: np.ndarray
+    count: np.ndarray
+    round: np.ndarray
+    n_rounds: int
+    round_elems: int
+
+    def own_counts(self, cls: DtypeClass, rank: int) -> list[int]:
+        """Elements of ``rank``'s segment each round reduces (its padded load, split)."""
+        S, n = self.round_elems, cls.own_len[rank]
+        return [max(0, min(S, n - k * S)) for k in range(self.n_rounds)]
+
+
+def round_elems_for(cls: DtypeClass, world: int, elem_bytes: int, budget_bytes: int) -> int:
+    """Largest round (multiple of ALIGN elements) whose double-buffered receive window of
+    ``world`` regions fits ``budget_bytes``, and no larger than one segment."""
+    s = budget_bytes // (2 * world * elem_bytes)
+    s = max(ALIGN, s // ALIGN * ALIGN)
+    return min(s, max(cls.seg_len, ALIGN))
+
+
+def exchange_pieces(cls: DtypeClass, owner: list[int], numels: list[int], round_elems: int) -> Pieces:
+    """Pieces of every tensor's slot, plus zero-fill pieces (``tensor`` -1) over the gaps
+    between slots up to each owner's padded load: the two halves of the receive window are
+    reused by rounds with different layouts, so every element an owner adds must be
+    rewritten by every round (a gap left untouched would still hold an older round's
+    values)."""
+    S = round_elems
+    assert S % ALIGN == 0
+    cols = [[] for _ in range(6)]
+
+    def emit(k, start, n, o, src0):
+        for r in range(start // S, (start + n - 1) // S + 1):
+            lo, hi = max(start, r * S), min(start + n, (r + 1) * S)
+            for col, val in zip(cols, (k, src0 + lo - start, o, lo - r * S, hi - lo, r)):
+                col.append(val)
+
+    ends = {}
+    for k, i in enumerate(cls.indices):
+        off, n, o = cls.offset[i], numels[i], owner[i]
+        if n:
+            emit(k, off, n, o, 0)
+        ends.setdefault(o, []).append((off, off + n))
+    for o, slots in ends.items():  # the gaps of owner o's segment, up to its padded load
+        pos = 0
+        for lo, hi in sorted(slots) + [(cls.own_len[o], cls.own_len[o])]:
+            if lo > pos:
+                emit(-1, pos, lo - pos, o, 0)
+            pos = max(pos, hi)
+    arr = [np.asarray(c, dtype=np.int64) for c in cols]
+    n_rounds = max(1, -(-cls.seg_len // S))
+    return Pieces(*arr, n_rounds=n_rounds, round_elems=S)
+
+
+def interleaved_chunks(entries: np.ndarray, entry_owner: np.ndarray, entry_numel: np.ndarray, rank: int, world: int,
+                       chunk_elems: int) -> np.ndarray:
+    """ha_chunk list over the given table entries, one chunk per owner in turn (starting
+    at owner rank+1, ending with this rank's own), as push_chunk_order explains."""
+    per_owner: list[list[tuple[int, int]]] = [[] for _ in range(world)]
+    for e in entries.tolist():
+        n_chunks = (int(entry_numel[e]) + chunk_elems - 1) // chunk_elems
+        per_owner[int(entry_owner[e])].extend((e, c) for c in range(n_chunks))
+    order = [(rank + d) % world for d in range(1, world + 1)]
+    out = []
+    pos = [0] * world
+    remaining = sum(len(x) for x in per_owner)
+    while remaining:
+        for o in order:
+            if pos[o] < len(per_owner[o]):
+                out.append(per_owner[o][pos[o]])
+                pos[o] += 1
+                remaining -= 1
+    tab = np.zeros(len(out), dtype=_lib.CHUNK_DTYPE)
+    if out:
+        tab["tensor"] = [k for k, _ in out]
+        tab["index"] = [c for _, c in out]
+    return tab
+
+
 def push_chunk_order(cls: DtypeClass, owner: list[int], rank: int, world: int, numels: list[int],
                      chunk_elems: int) -> np.ndarray:
     """ha_chunk list of the gradient push, interleaved across destination owners.

@@ -147,14 +147,17 @@ class _Class:
         dev = opt.device
         W, r = opt.world, opt.rank
         numel = opt._numels
-        # --- packed parameter / gradient buffers (world > 1), IPC-shareable
-        self.packed_param = self.packed_grad = None
+        # --- packed parameters and the gradient receive window (world > 1), IPC-shareable;
+        # the reduced-gradient buffer depends on the mode (set_mode)
+        self.packed_param = None
         if W > 1:
             from .p2p import DeviceBuffer
             self.param_buf = DeviceBuffer(W * cls.seg_len, self.dtype, dev)
-            self.grad_buf = DeviceBuffer(W * cls.seg_len, self.dtype, dev)
             self.packed_param = self.param_buf.tensor
-            self.packed_grad = self.grad_buf.tensor
+            esz = self.packed_param.element_size()
+            budget = int(os.environ.get("HYBRIDAGENT_B200_RECV_BYTES", str(2 << 30)))
+            self.round_elems = layout.round_elems_for(cls, W, esz, budget)
+            self.recv_buf = DeviceBuffer(2 * W * self.round_elems, self.dtype, dev)
             for i in cls.indices:
                 p = opt.params[i]
                 start = opt.owner[i] * cls.seg_len + cls.offset[i]
@@ -192,40 +195,63 @@ class _Class:
         self.adamw_chunks = self._device_chunks(owned_numels, HA_ADAMW_CHUNK, dev)
         self.sumsq_chunks = self._device_chunks(owned_numels, HA_SUMSQ_CHUNK, dev)
         self.partials = torch.empty(max(self.sumsq_chunks[1], 1), dtype=torch.float64, device=dev)
-        # --- gradient move table (world > 1): every tensor of the class -> where this rank's
-        # gradient goes (p2p: the owner's receive region of this rank; nccl: its slot in the
-        # local owner-major pack); destinations are set by set_destinations()
         self.move = None
-        if W > 1:
-            self.move = _Table(len(cls.indices), _lib.COPY_DTYPE, dev)
-            for k, i in enumerate(cls.indices):
-                self.move.np[k]["numel"] = numel[i]
-            self.move_chunks = self._device_chunks([numel[i] for i in cls.indices], HA_ADAMW_CHUNK, dev)
-            # reduced gradients handed to the caller as p.grad (optimizer.py:141): the owner's own
-            # segment of the gradient buffer in both modes
-            own0 = r * cls.seg_len
-            self.grad_view = {i: self.packed_grad[own0 + cls.offset[i]:own0 + cls.offset[i] + numel[i]]
-                              .view(opt.params[i].shape) for i in self.owned}
-            n_regions = max((cls.own_len[r] + HA_SUM_REGIONS_CHUNK - 1) // HA_SUM_REGIONS_CHUNK, 1)
-            self.region_partials = torch.empty(n_regions, dtype=torch.float64, device=dev)
-            self.peers = _lib.Peers()
-
-    def set_destinations(self, opt: "ZeroOneAdamW", grad_bases: list[int] | None,
-                         param_bases: list[int] | None) -> None:
-        """p2p when the peers' buffer addresses are given, else the local nccl pack."""
-        dst = layout.push_destinations(self.layout, opt.owner, opt.rank, self.packed_grad.element_size(),
-                                       grad_bases, self.packed_grad.data_ptr())
-        self.move.np["dst"][:len(dst)] = dst
-        if grad_bases is not None:  # p2p: interleave the push across destination owners
-            order = layout.push_chunk_order(self.layout, opt.owner, opt.rank, opt.world, opt._numels,
-                                            HA_ADAMW_CHUNK)
-            self.move_chunks = (torch.from_numpy(order.view(np.uint8).copy()).to(opt.device), len(order))
         self.peers = _lib.Peers()
-        if param_bases is not None:
-            deltas = layout.peer_deltas(param_bases, opt.rank)
+
+    def set_mode(self, opt: "ZeroOneAdamW", recv_bases: list[int] | None, param_bases: list[int] | None) -> None:
+        """p2p (peers' receive windows and parameter buffers mapped) or the local nccl pack.
+
+        p2p: this rank's gradients move to their owners in rounds (layout.exchange_pieces):
+        round k covers elements [k*S, (k+1)*S) of every owner's segment and lands in half
+        k % 2 of the owner's double-buffered receive window, region <this rank>; the owner
+        adds the regions into ``own_grad``.  nccl: the whole owner-major pack of W segments
+        is reduce-scattered in place."""
+        cls, W, r, dev = self.layout, opt.world, opt.rank, opt.device
+        numel = opt._numels
+        esz = self.packed_param.element_size()
+        if recv_bases is not None:
+            S = self.round_elems
+            pc = layout.exchange_pieces(cls, opt.owner, numel, S)
+            self.pieces = pc
+            self.own_grad = torch.zeros(max(cls.own_len[r], layout.ALIGN), dtype=self.dtype, device=dev)
+            base = self.own_grad
+            own0 = 0
+            self.move = _Table(len(pc.count), _lib.COPY_DTYPE, dev)
+            bases = np.asarray(recv_bases, dtype=np.uint64)
+            dst = bases[pc.owner] + (((pc.round % 2) * W * S + r * S + pc.dst_off) * esz).astype(np.uint64)
+            self.move.np["dst"][:len(dst)] = dst
+            self.move.np["numel"][:len(dst)] = pc.count
+            self.piece_tensor = pc.tensor
+            self.piece_src_bytes = (pc.src_off * esz).astype(np.uint64)
+            self.round_chunks = []
+            for k in range(pc.n_rounds):
+                entries = np.nonzero(pc.round == k)[0]
+                tab = layout.interleaved_chunks(entries, pc.owner, pc.count, r, W, HA_ADAMW_CHUNK)
+                _lib.call("ha_check_chunks", len(pc.count), _lib.np_ptr(np.ascontiguousarray(pc.count)),
+                          _lib.np_ptr(tab), len(tab), HA_ADAMW_CHUNK)
+                self.round_chunks.append((torch.from_numpy(tab.view(np.uint8).copy()).to(dev) if len(tab) else None,
+                                          len(tab)))
+            self.own_counts = pc.own_counts(cls, r)
+            self.region_partials = torch.empty(max(-(-S // HA_SUM_REGIONS_CHUNK), 1), dtype=torch.float64,
+                                               device=dev)
+            self.peers = _lib.Peers()
+            deltas = layout.peer_deltas(param_bases, r)
             for q, d in enumerate(deltas):
                 self.peers.delta[q] = d
             self.peers.n = len(deltas)
+        else:
+            self.recv_buf = None  # not used without peer mappings
+            self.grad_buf = torch.zeros(W * cls.seg_len, dtype=self.dtype, device=dev)
+            base = self.grad_buf
+            own0 = r * cls.seg_len
+            self.move = _Table(len(cls.indices), _lib.COPY_DTYPE, dev)
+            dst = layout.push_destinations(cls, opt.owner, r, esz, None, self.grad_buf.data_ptr())
+            self.move.np["dst"][:len(dst)] = dst
+            self.move.np["numel"][:len(dst)] = [numel[i] for i in cls.indices]
+            self.move_chunks = self._device_chunks([numel[i] for i in cls.indices], HA_ADAMW_CHUNK, dev)
+        # reduced gradients handed to the caller as p.grad (optimizer.py:141)
+        self.grad_view = {i: base[own0 + cls.offset[i]:own0 + cls.offset[i] + numel[i]].view(opt.params[i].shape)
+                          for i in self.owned}
 
     @staticmethod
     def _device_chunks(numels: list[int], chunk: int, dev) -> tuple[torch.Tensor | None, int]:
@@ -329,7 +355,7 @@ class ZeroOneAdamW:
             from .p2p import PeerMap
             bufs = {}
             for k, c in enumerate(self._classes):
-                bufs[f"grad{k}"] = c.grad_buf
+                bufs[f"recv{k}"] = c.recv_buf
                 bufs[f"param{k}"] = c.param_buf
             self._peer_map = PeerMap(bufs, self.rank, self.world)
             ok = 1 if self._peer_map.ok else 0
@@ -343,10 +369,45 @@ class ZeroOneAdamW:
         self.comm_mode = "p2p" if use_p2p else "nccl"
         for k, c in enumerate(self._classes):
             if use_p2p:
-                c.set_destinations(self, self._peer_map.bases[f"grad{k}"], self._peer_map.bases[f"param{k}"])
+                c.set_mode(self, self._peer_map.bases[f"recv{k}"], self._peer_map.bases[f"param{k}"])
             else:
-                c.set_destinations(self, None, None)
+                c.set_mode(self, None, None)
             c.move.upload()
+        rounds = max(c.pieces.n_rounds for c in self._classes) if use_p2p else 1
+        self._norm_rounds = torch.zeros((len(self._classes), rounds), dtype=torch.float64, device=self.device)
+        self._norm_rounds_host = torch.zeros((len(self._classes), rounds), dtype=torch.float64, pin_memory=True)
+
+    def _exchange_rounds(self) -> None:
+        """p2p gradient exchange: per round, every rank pushes its pieces into the owners'
+        receive windows, one barrier, then each owner adds the regions of that round into
+        its reduced gradients and the norm's square sums.  Double buffering (half k % 2)
+        makes one barrier per round enough: a rank pushes into a half again only after the
+        next round's barrier, which every owner enters after summing that half."""
+        rounds = max(c.pieces.n_rounds for c in self._classes)
+        for k in range(rounds):
+            self._phase("push", True)
+            for c in self._classes:
+                if k < c.pieces.n_rounds and c.round_chunks[k][1]:
+                    ch, n = c.round_chunks[k]
+                    _lib.call("ha_gather", c.move.ptr, ch.data_ptr(), n, HA_ADAMW_CHUNK,
+                              c.packed_param.element_size(), self._stream())
+                    self.launches += 1
+            self._phase("push", False)
+            self._phase("barrier", True)
+            self._barrier()  # every rank's pushes of this round have landed
+            self._phase("barrier", False)
+            self._phase("sum_regions", True)
+            for ci, c in enumerate(self._classes):
+                if k >= c.pieces.n_rounds:
+                    continue
+                S, esz = c.round_elems, c.packed_param.element_size()
+                count = c.own_counts[k]
+                window = c.recv_buf.ptr + (k % 2) * self.world * S * esz
+                _lib.call("ha_sum_regions", window, self.world, S, count, c.own_grad.data_ptr() + k * S * esz,
+                          c.code, c.region_partials.data_ptr(), self._norm_rounds[ci, k:].data_ptr(),
+                          self._stream())
+                self.launches += 2 if count else 1
+            self._phase("sum_regions", False)
 
     def _barrier(self) -> None:
         """Stream-ordered barrier across ranks: returns on every rank's stream only after every
@@ -431,8 +492,9 @@ class ZeroOneAdamW:
             used = self._comm.read(self._used_dev, self._used_host, "all-reduce(max) of the used mask")
             used = used.numpy().astype(bool)
             keep = []  # gradients that must stay alive until the move kernel has read them
+            p2p = self.comm_mode == "p2p"
             for c in self._classes:
-                cp = c.move.np
+                ptrs = np.zeros(len(c.layout.indices), dtype=np.uint64)
                 for k, i in enumerate(c.layout.indices):
                     p = self.params[i]
                     if p.data.data_ptr() != c.packed_param.data_ptr() + (
@@ -440,39 +502,33 @@ class ZeroOneAdamW:
                         raise RuntimeError(f"parameter {i} was re-bound after the optimizer was built")
                     g = p.grad
                     if g is None or not used[i]:
-                        cp[k]["src"] = 0  # contributes zeros (optimizer.py:131-132)
-                        continue
+                        continue  # contributes zeros (optimizer.py:131-132)
                     if g.dtype != c.dtype or g.numel() != self._numels[i] or g.device != self.device:
                         raise RuntimeError(f"gradient of tensor {i}: {g.dtype} x {g.numel()} on {g.device}")
                     if not g.is_contiguous():
                         g = g.contiguous()
                     keep.append(g)
-                    cp[k]["src"] = g.data_ptr()  # equal to dst when the gradient already lives in its slot
+                    ptrs[k] = g.data_ptr()
+                if p2p:  # each piece reads its part of its tensor's gradient (0: zero-fill; -1: a gap)
+                    pt = np.where(c.piece_tensor >= 0, ptrs[np.maximum(c.piece_tensor, 0)], 0).astype(np.uint64)
+                    c.move.np["src"][:len(pt)] = np.where(pt != 0, pt + c.piece_src_bytes, 0)
+                else:  # equal to dst when the gradient already lives in its slot
+                    c.move.np["src"][:len(ptrs)] = ptrs
                 c.move.upload()
-            p2p = self.comm_mode == "p2p"
-            self._phase("push" if p2p else "pack", True)
-            for c in self._classes:
-                if c.move_chunks[1]:
-                    _lib.call("ha_gather", c.move.ptr, c.move_chunks[0].data_ptr(), c.move_chunks[1], HA_ADAMW_CHUNK,
-                              c.packed_grad.element_size(), self._stream())
-                    self.launches += 1
-            self._phase("push" if p2p else "pack", False)
             if p2p:
-                self._phase("barrier", True)
-                self._barrier()  # every rank's pushes have landed
-                self._phase("barrier", False)
-                self._phase("sum_regions", True)
-                for k, c in enumerate(self._classes):
-                    _lib.call("ha_sum_regions", c.grad_buf.ptr, self.world, self.rank, c.layout.seg_len,
-                              c.layout.own_len[self.rank], c.code, c.region_partials.data_ptr(),
-                              self._norm_buf[k:].data_ptr(), self._stream())
-                    self.launches += 2 if c.layout.own_len[self.rank] else 1
-                self._phase("sum_regions", False)
+                self._exchange_rounds()
             else:
+                self._phase("pack", True)
+                for c in self._classes:
+                    if c.move_chunks[1]:
+                        _lib.call("ha_gather", c.move.ptr, c.move_chunks[0].data_ptr(), c.move_chunks[1],
+                                  HA_ADAMW_CHUNK, c.grad_buf.element_size(), self._stream())
+                        self.launches += 1
+                self._phase("pack", False)
                 self._phase("reduce_scatter", True)
                 for c in self._classes:
-                    own = c.packed_grad.data_ptr() + self.rank * c.layout.seg_len * c.packed_grad.element_size()
-                    self._comm.reduce_scatter(c.packed_grad.data_ptr(), own, c.layout.seg_len, c.code)
+                    own = c.grad_buf.data_ptr() + self.rank * c.layout.seg_len * c.grad_buf.element_size()
+                    self._comm.reduce_scatter(c.grad_buf.data_ptr(), own, c.layout.seg_len, c.code)
                 self._phase("reduce_scatter", False)
             del keep
             self._grad_cache = {}
@@ -510,7 +566,11 @@ class ZeroOneAdamW:
                               self._stream())
                     self.launches += 2 if n else 1
                 self._phase("sumsq", False)
-            if self.world > 1:
+            if self.world > 1 and reuse:  # the exchange's square sums, one per class and round
+                self._comm.all_reduce_sum(self._norm_rounds, HA_F64)
+                partial = self._comm.read(self._norm_rounds, self._norm_rounds_host,
+                                          "all-reduce(sum) of the norm").reshape(-1).tolist()
+            elif self.world > 1:
                 self._comm.all_reduce_sum(self._norm_buf, HA_F64)
                 partial = self._comm.read(self._norm_buf, self._norm_host, "all-reduce(sum) of the norm").tolist()
             else:

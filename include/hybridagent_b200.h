@@ -167,9 +167,11 @@ int ha_scale_grads(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t
                    int grad_dtype, float mult, void* stream);
 
 /* Multi-tensor copy / zero-fill (replaces the bucket packing of optimizer.py:126-135).
- * chunk_elems elements of elem_bytes (2 or 4) per chunk. */
+ * chunk_elems elements of elem_bytes (2 or 4) per chunk.  Destinations may be peer-mapped
+ * memory (the p2p gradient push). */
 int ha_gather(const ha_copy* d_copies, const ha_chunk* d_chunks, int64_t n_chunks, int64_t chunk_elems,
               int elem_bytes, void* stream);
+
 
 /* ------------------------------------------------------------------ peer-to-peer (NVLink / NVSwitch) */
 
@@ -194,10 +196,11 @@ int ha_ipc_close(void* ptr);
  * the norm's square-sum of :149-151 in one pass): d_regions holds `world` regions of
  * region_elems elements, region r written by rank r's push (ha_gather into the owner's
  * receive buffer).  Elements [0, count) of all regions are added in fp32 in rank order
- * 0..world-1, rounded once to dtype and written over region `rank`; the sum of squares of
- * the written values goes to d_partials (one per HA_SUM_REGIONS_CHUNK) and d_out[0].  At
- * world 2 this equals any SUM reduction of the two gradients bit for bit. */
-int ha_sum_regions(void* d_regions, int32_t world, int32_t rank, int64_t region_elems, int64_t count, int dtype,
+ * 0..world-1, rounded once to dtype and written to d_sum[0, count) (which may alias one
+ * region); the sum of squares of the written values goes to d_partials (one per
+ * HA_SUM_REGIONS_CHUNK) and d_out[0].  At world 2 this equals any SUM reduction of the two
+ * gradients bit for bit. */
+int ha_sum_regions(const void* d_regions, int32_t world, int64_t region_elems, int64_t count, void* d_sum, int dtype,
                    double* d_partials, double* d_out, void* stream);
 
 /* ha_adamw_step that also stores every updated parameter value (the low-precision copy,

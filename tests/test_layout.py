@@ -65,3 +65,41 @@ def test_push_destinations_land_in_the_senders_region():
             assert elem == rank * cls.seg_len + cls.offset[i]
             assert elem + n[i] <= (rank + 1) * cls.seg_len
     assert layout.peer_deltas([100, 300, 700], 1) == [-200, 400]
+
+
+@pytest.mark.parametrize("world,S", [(2, 64 * 1000), (3, 64 * 7), (8, 64 * 50_000), (2, 64)])
+def test_exchange_pieces_partition_every_slot_and_gap(world, S):
+    import numpy as np
+    n = [1000, 64, 5000, 3, 70000, 1, 12345, 640000]
+    p = layout.plan(n, [HA_BF16] * len(n), world)
+    (cls,) = p.classes
+    pc = layout.exchange_pieces(cls, p.owner, n, S)
+    assert pc.n_rounds == -(-cls.seg_len // S)
+    covered = {i: np.zeros(n[i], np.int32) for i in cls.indices}
+    # what each owner's region receives in each round, from every piece (tensors and gaps)
+    written = {(o, r): np.zeros(S, np.int32) for o in range(world) for r in range(pc.n_rounds)}
+    for t, so, o, do, c, r in zip(pc.tensor, pc.src_off, pc.owner, pc.dst_off, pc.count, pc.round):
+        assert 0 < c and 0 <= do and do + c <= S
+        written[(o, r)][do:do + c] += 1
+        if t < 0:
+            continue  # a zero-filled gap
+        i = cls.indices[t]
+        assert o == p.owner[i]
+        assert cls.offset[i] + so == r * S + do  # same segment coordinate
+        covered[i][so:so + c] += 1
+    assert all((v == 1).all() for v in covered.values())
+    for o in range(world):
+        counts = pc.own_counts(cls, o)
+        assert sum(counts) == cls.own_len[o] and all(0 <= x <= S for x in counts)
+        for r in range(pc.n_rounds):
+            w = written[(o, r)]
+            assert (w[:counts[r]] == 1).all() and (w[counts[r]:] == 0).all()  # every summed element, once
+
+
+def test_round_elems_for_budget():
+    n = workloads.numels(workloads.qwen3_8b())
+    p = layout.plan(n, [HA_BF16] * len(n), 8)
+    (cls,) = p.classes
+    S = layout.round_elems_for(cls, 8, 2, 2 << 30)
+    assert S % layout.ALIGN == 0 and 2 * 8 * S * 2 <= 2 << 30
+    assert layout.round_elems_for(cls, 8, 2, 1 << 60) == cls.seg_len

@@ -31,10 +31,12 @@ def _gpus() -> int:
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("mode", ["p2p", "nccl"])
+@pytest.mark.parametrize("mode", ["p2p", "p2p_rounds", "nccl"])
 @pytest.mark.parametrize("name", ["bf16_world2", "fp32_world2", "bf16_world2_inf"])
 def test_world2_matches_oracle_and_reference(name, mode, tmp_path):
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", HYBRIDAGENT_B200_COMM=mode)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", HYBRIDAGENT_B200_COMM=mode.split("_")[0])
+    if mode == "p2p_rounds":  # a 16 KiB receive window: ~9 exchange rounds of 1024 elements
+        env["HYBRIDAGENT_B200_RECV_BYTES"] = "16384"
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29731",
            os.path.join(HERE, "world_worker.py"), name, str(tmp_path)]
@@ -43,7 +45,7 @@ def test_world2_matches_oracle_and_reference(name, mode, tmp_path):
     res = [pickle.load(open(tmp_path / f"rank{r}.pkl", "rb")) for r in range(2)]
     case = CASES_BY_NAME[name]
     g = golden(name)
-    assert res[0]["mode"] == res[1]["mode"] == mode
+    assert res[0]["mode"] == res[1]["mode"] == mode.split("_")[0]
     assert res[0]["norms"] == res[1]["norms"]
     assert res[0]["owner"] == g["owner"].tolist()
     for s, (mine, ref) in enumerate(zip(res[0]["norms"], g["norms"].tolist())):

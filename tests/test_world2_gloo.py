@@ -165,12 +165,13 @@ def test_world2_host_path_matches_reference(name):
 
 
 def _rank_main_p2p(rank, world, port, name, queue):
-    """The p2p data flow: each rank pushes every gradient to the address
-    layout.push_destinations gives (in the owner's receive buffer, region <rank>), the owner
-    adds the regions in rank order and clips / updates its slots, and each new parameter is
-    stored at layout.peer_deltas offsets into every peer's packed parameters.  Device
-    memories are simulated as numpy arrays at fake base addresses; the stores that cross
-    ranks travel through gloo."""
+    """The p2p data flow: in rounds (layout.exchange_pieces, a small round size so slots
+    straddle rounds), each rank pushes each piece of its gradients to the address the
+    product computes (half round % 2 of the owner's receive window, region <rank>), the
+    owner adds the regions of the round in rank order into its reduced gradients, clips and
+    updates its slots, and each new parameter is stored at layout.peer_deltas offsets into
+    every peer's packed parameters.  Device memories are simulated as numpy arrays at fake
+    base addresses; the stores that cross ranks travel through gloo."""
     import sys
     sys.path[:0] = [os.path.dirname(os.path.dirname(os.path.abspath(__file__))), os.path.dirname(__file__),
                     os.path.join(os.path.dirname(__file__), "golden")]
@@ -194,14 +195,16 @@ def _rank_main_p2p(rank, world, port, name, queue):
         npdt = np.uint16 if case.dtype == Z.BF16 else np.float32
         esz = np.dtype(npdt).itemsize
         SPACE = 1 << 40
-        grad_bases = [(r + 1) * SPACE for r in range(world)]            # each rank's receive buffer
+        S = 64 * 20  # small rounds: slots straddle rounds and both halves of the window are used
+        recv_bases = [(r + 1) * SPACE for r in range(world)]               # each rank's receive window
         param_bases = [(r + 1) * SPACE + SPACE // 2 for r in range(world)]  # each rank's packed params
-        dst = layout.push_destinations(cls, plan.owner, rank, esz, grad_bases, 0)
+        pieces = layout.exchange_pieces(cls, plan.owner, numels, S)
+        assert pieces.n_rounds > 4
         deltas = layout.peer_deltas(param_bases, rank)
         peers = [r for r in range(world) if r != rank]
 
         def exchange(images):
-            """images[r]: this rank's stores into rank r's memory (NaN / sentinel = untouched)."""
+            """images[r]: this rank's stores into rank r's memory."""
             everyone = [None] * world
             dist.all_gather_object(everyone, images)
             return [everyone[s][rank] for s in range(world)]
@@ -214,31 +217,41 @@ def _rank_main_p2p(rank, world, port, name, queue):
         owned = cls.owned(plan.owner, rank)
         state = {i: [Z.widen(init[i], case.dtype).copy(), np.zeros(numels[i], np.float32),
                      np.zeros(numels[i], np.float32), 0] for i in owned}
-        recv = np.zeros(world * seg, npdt)
+        window = np.zeros(2 * world * S, npdt)  # this rank's double-buffered receive window
+        own = np.zeros(max(cls.own_len[rank], 1), npdt)
         norms = []
         for s in range(case.steps):
             grads = case.grads(s, rank)
             used = torch.tensor([g is not None for g in grads], dtype=torch.uint8)
             dist.all_reduce(used, op=dist.ReduceOp.MAX)
-            # push: write each gradient (zeros when absent) at its destination address
-            images = [dict() for _ in range(world)]
-            for k, i in enumerate(cls.indices):
-                owner = plan.owner[i]
-                elem = (dst[k] - grad_bases[owner]) // esz
-                assert rank * seg <= elem and elem + numels[i] <= (rank + 1) * seg  # region <rank> of the owner
-                g = grads[i] if grads[i] is not None and used[i] else np.zeros(numels[i], npdt)
-                images[owner][elem] = g
-            for img in exchange(images):
-                for elem, g in img.items():
-                    recv[elem:elem + len(g)] = g
-            # owner: add the regions in rank order, round once, square sums of the result
-            acc = Z.widen(recv[0:seg].copy(), case.dtype)
-            for r in range(1, world):
-                acc = acc + Z.widen(recv[r * seg:(r + 1) * seg], case.dtype)
-            own = Z.narrow(acc, case.dtype) if case.dtype != Z.F32 else acc.astype(np.float32)
-            recv[rank * seg:(rank + 1) * seg] = own
+            for k in range(pieces.n_rounds):
+                # push round k: each piece at the address the product computes for it
+                images = [dict() for _ in range(world)]
+                for j in np.nonzero(pieces.round == k)[0]:
+                    t = int(pieces.tensor[j])
+                    o, so, c = int(pieces.owner[j]), int(pieces.src_off[j]), int(pieces.count[j])
+                    addr = recv_bases[o] + ((k % 2) * world * S + rank * S + int(pieces.dst_off[j])) * esz
+                    elem = (addr - recv_bases[o]) // esz
+                    assert (k % 2) * world * S + rank * S <= elem and elem + c <= (k % 2) * world * S + (rank + 1) * S
+                    if t < 0:  # a gap between slots: zeros
+                        images[o][elem] = np.zeros(c, npdt)
+                        continue
+                    i = cls.indices[t]
+                    g = grads[i] if grads[i] is not None and used[i] else np.zeros(numels[i], npdt)
+                    images[o][elem] = g[so:so + c]
+                for img in exchange(images):
+                    for elem, g in img.items():
+                        window[elem:elem + len(g)] = g
+                # owner: add the regions of this half in rank order, round once
+                count = pieces.own_counts(cls, rank)[k]
+                half = (k % 2) * world * S
+                acc = Z.widen(window[half:half + count].copy(), case.dtype)
+                for r in range(1, world):
+                    acc = acc + Z.widen(window[half + r * S:half + r * S + count], case.dtype)
+                own[k * S:k * S + count] = Z.narrow(acc, case.dtype) if case.dtype != Z.F32 else acc
             mine = {i: own[cls.offset[i]:cls.offset[i] + numels[i]].copy() for i in owned if used[i]}
-            total = torch.tensor([sum(Z.sumsq(g, case.dtype) for g in mine.values())], dtype=torch.float64)
+            # like the product's fused sums: the whole reduced region, gaps included (all zero)
+            total = torch.tensor([Z.sumsq(own[:cls.own_len[rank]].copy(), case.dtype)], dtype=torch.float64)
             dist.all_reduce(total)
             norm = Z.norm_from_sumsq(float(total))
             norms.append(norm)
