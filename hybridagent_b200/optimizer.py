@@ -155,7 +155,7 @@ class _Class:
             self.param_buf = DeviceBuffer(W * cls.seg_len, self.dtype, dev)
             self.packed_param = self.param_buf.tensor
             esz = self.packed_param.element_size()
-            budget = int(os.environ.get("HYBRIDAGENT_B200_RECV_BYTES", str(2 << 30)))
+            budget = int(os.environ.get("HYBRIDAGENT_B200_RECV_BYTES", str(4 << 30)))
             self.round_elems = layout.round_elems_for(cls, W, esz, budget)
             self.recv_buf = DeviceBuffer(2 * W * self.round_elems, self.dtype, dev)
             for i in cls.indices:
@@ -485,30 +485,38 @@ class ZeroOneAdamW:
             return
         self.apply_pending_clip()
         with torch.cuda.device(self.device):
-            local = np.fromiter((p.grad is not None for p in self.params), dtype=np.uint8, count=len(self.params))
-            self._used_dev.copy_(torch.from_numpy(local), non_blocking=False)
-            self._comm.all_reduce_max(self._used_dev, HA_U8)
-            # a rank that stopped answering ends here (CommFailure), before any peer store
-            used = self._comm.read(self._used_dev, self._used_host, "all-reduce(max) of the used mask")
-            used = used.numpy().astype(bool)
+            # everything that reads the parameters' Python attributes happens before the mask is
+            # synchronised, overlapping the GPU's earlier work (it dominates with ~10^4 tensors)
             keep = []  # gradients that must stay alive until the move kernel has read them
             p2p = self.comm_mode == "p2p"
+            local = np.zeros(len(self.params), dtype=np.uint8)
+            class_ptrs = []
             for c in self._classes:
                 ptrs = np.zeros(len(c.layout.indices), dtype=np.uint64)
+                esz = c.packed_param.element_size()
+                base = c.packed_param.data_ptr()
                 for k, i in enumerate(c.layout.indices):
                     p = self.params[i]
-                    if p.data.data_ptr() != c.packed_param.data_ptr() + (
-                            self.owner[i] * c.layout.seg_len + c.layout.offset[i]) * p.element_size():
+                    if p.data.data_ptr() != base + (self.owner[i] * c.layout.seg_len + c.layout.offset[i]) * esz:
                         raise RuntimeError(f"parameter {i} was re-bound after the optimizer was built")
                     g = p.grad
-                    if g is None or not used[i]:
-                        continue  # contributes zeros (optimizer.py:131-132)
+                    if g is None:
+                        continue
+                    local[i] = 1
                     if g.dtype != c.dtype or g.numel() != self._numels[i] or g.device != self.device:
                         raise RuntimeError(f"gradient of tensor {i}: {g.dtype} x {g.numel()} on {g.device}")
                     if not g.is_contiguous():
                         g = g.contiguous()
                     keep.append(g)
                     ptrs[k] = g.data_ptr()
+                class_ptrs.append(ptrs)
+            self._used_dev.copy_(torch.from_numpy(local), non_blocking=False)
+            self._comm.all_reduce_max(self._used_dev, HA_U8)
+            # a rank that stopped answering ends here (CommFailure), before any peer store
+            used = self._comm.read(self._used_dev, self._used_host, "all-reduce(max) of the used mask")
+            used = used.numpy().astype(bool)
+            for c, ptrs in zip(self._classes, class_ptrs):
+                ptrs[~used[np.asarray(c.layout.indices)]] = 0  # unused everywhere: zeros (optimizer.py:111-114)
                 if p2p:  # each piece reads its part of its tensor's gradient (0: zero-fill; -1: a gap)
                     pt = np.where(c.piece_tensor >= 0, ptrs[np.maximum(c.piece_tensor, 0)], 0).astype(np.uint64)
                     c.move.np["src"][:len(pt)] = np.where(pt != 0, pt + c.piece_src_bytes, 0)
