@@ -200,3 +200,23 @@ def test_apply_pending_clip_scales_strided_gradients_in_place():
     want = g.copy()
     Z.clip_inplace(want, Z.BF16, Z.FORM_TORCH_CUDA, 1.0 / (n + 1e-6))
     assert_bits_equal(to_numpy(p.grad, Z.BF16), want, "strided clipped grad")
+
+
+def test_checkpoint_files_resume_bit_identically(tmp_path):
+    import torch
+    from hybridagent_b200 import ZeroOneAdamW
+    from hybridagent_b200.checkpoint import load_optimizer_state, save_optimizer_state
+    case = next(c for c in CASES if c.name == "bf16_sparse")
+    params, opt = build(case)
+    run_steps(case, params, opt, range(2))
+    save_optimizer_state(opt, tmp_path / "checkpoint-2")
+    fresh = [torch.nn.Parameter(p.detach().clone()) for p in params]
+    opt2 = ZeroOneAdamW([{"params": fresh, "lr": case.lr}], rank=0, world_size=1, betas=case.betas, eps=case.eps,
+                        weight_decay=case.weight_decay)
+    load_optimizer_state(opt2, tmp_path / "checkpoint-2")
+    run_steps(case, params, opt, [2])
+    run_steps(case, fresh, opt2, [2])
+    for i in range(len(params)):
+        assert torch.equal(params[i].data, fresh[i].data)
+        assert torch.equal(opt.exp_avg_sq[i], opt2.exp_avg_sq[i]) and torch.equal(opt.master[i], opt2.master[i])
+        assert opt.param_steps[i] == opt2.param_steps[i]
