@@ -232,8 +232,8 @@ class _Class:
                 self.round_chunks.append((torch.from_numpy(tab.view(np.uint8).copy()).to(dev) if len(tab) else None,
                                           len(tab)))
             self.own_counts = pc.own_counts(cls, r)
-            self.region_partials = torch.empty(max(-(-S // HA_SUM_REGIONS_CHUNK), 1), dtype=torch.float64,
-                                               device=dev)
+            n_part = max(-(-S // HA_SUM_REGIONS_CHUNK), 1)
+            self.region_partials = [torch.empty(n_part, dtype=torch.float64, device=dev) for _ in range(2)]
             self.peers = _lib.Peers()
             deltas = layout.peer_deltas(param_bases, r)
             for q, d in enumerate(deltas):
@@ -373,6 +373,7 @@ class ZeroOneAdamW:
             else:
                 c.set_mode(self, None, None)
             c.move.upload()
+        self._sum_stream = torch.cuda.Stream(device=self.device) if use_p2p else None
         rounds = max(c.pieces.n_rounds for c in self._classes) if use_p2p else 1
         self._norm_rounds = torch.zeros((len(self._classes), rounds), dtype=torch.float64, device=self.device)
         self._norm_rounds_host = torch.zeros((len(self._classes), rounds), dtype=torch.float64, pin_memory=True)
@@ -380,34 +381,50 @@ class ZeroOneAdamW:
     def _exchange_rounds(self) -> None:
         """p2p gradient exchange: per round, every rank pushes its pieces into the owners'
         receive windows, one barrier, then each owner adds the regions of that round into
-        its reduced gradients and the norm's square sums.  Double buffering (half k % 2)
-        makes one barrier per round enough: a rank pushes into a half again only after the
-        next round's barrier, which every owner enters after summing that half."""
+        its reduced gradients and the norm's square sums.
+
+        The sums run on a second stream so round k's sum (HBM) overlaps round k+1's push
+        (NVLink).  The window is double-buffered (half k % 2): barrier k+1 is enqueued only
+        after this rank's sum k has finished, so when barrier k+1 completes every owner has
+        read half k % 2 and round k+2 may overwrite it; sum k waits for barrier k, so it reads
+        only after every rank's round-k pushes landed."""
+        main = torch.cuda.current_stream()
+        side = self._sum_stream
         rounds = max(c.pieces.n_rounds for c in self._classes)
+        summed = None  # event after the previous round's sums on the side stream
         for k in range(rounds):
             self._phase("push", True)
             for c in self._classes:
                 if k < c.pieces.n_rounds and c.round_chunks[k][1]:
                     ch, n = c.round_chunks[k]
                     _lib.call("ha_gather", c.move.ptr, ch.data_ptr(), n, HA_ADAMW_CHUNK,
-                              c.packed_param.element_size(), self._stream())
+                              c.packed_param.element_size(), main.cuda_stream)
                     self.launches += 1
             self._phase("push", False)
+            if summed is not None:
+                main.wait_event(summed)  # this rank has read the half that round k+1 rewrites
             self._phase("barrier", True)
-            self._barrier()  # every rank's pushes of this round have landed
+            self._barrier()  # every rank's pushes of round k have landed
             self._phase("barrier", False)
-            self._phase("sum_regions", True)
-            for ci, c in enumerate(self._classes):
-                if k >= c.pieces.n_rounds:
-                    continue
-                S, esz = c.round_elems, c.packed_param.element_size()
-                count = c.own_counts[k]
-                window = c.recv_buf.ptr + (k % 2) * self.world * S * esz
-                _lib.call("ha_sum_regions", window, self.world, S, count, c.own_grad.data_ptr() + k * S * esz,
-                          c.code, c.region_partials.data_ptr(), self._norm_rounds[ci, k:].data_ptr(),
-                          self._stream())
-                self.launches += 2 if count else 1
-            self._phase("sum_regions", False)
+            landed = torch.cuda.Event()
+            landed.record(main)
+            side.wait_event(landed)
+            with torch.cuda.stream(side):
+                self._phase("sum_regions", True)
+                for ci, c in enumerate(self._classes):
+                    if k >= c.pieces.n_rounds:
+                        continue
+                    S, esz = c.round_elems, c.packed_param.element_size()
+                    count = c.own_counts[k]
+                    window = c.recv_buf.ptr + (k % 2) * self.world * S * esz
+                    _lib.call("ha_sum_regions", window, self.world, S, count, c.own_grad.data_ptr() + k * S * esz,
+                              c.code, c.region_partials[k % 2].data_ptr(), self._norm_rounds[ci, k:].data_ptr(),
+                              side.cuda_stream)
+                    self.launches += 2 if count else 1
+                self._phase("sum_regions", False)
+            summed = torch.cuda.Event()
+            summed.record(side)
+        main.wait_event(summed)  # the reduced gradients and square sums are complete for later work
 
     def _barrier(self) -> None:
         """Stream-ordered barrier across ranks: returns on every rank's stream only after every

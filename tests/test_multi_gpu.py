@@ -87,3 +87,43 @@ def test_stalled_peer_raises_comm_failure(tmp_path):
     assert r0["error"] is not None and "did not complete within 5 s" in r0["error"], logs
     assert 5.0 <= r0["elapsed"] < 60.0, logs
     assert r1["error"] == "peer reported CommFailure before this rank's next launch", logs
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("mode", ["p2p", "p2p_rounds", "nccl"])
+def test_world2_mixed_dtype_classes(mode, tmp_path):
+    """bf16 + fp32 + fp16 parameters in one optimizer (three dtype classes, each exchanged
+    in its own rounds), a tensor absent on one rank: bit for bit against the oracle."""
+    sys.path.insert(0, HERE)
+    from world_worker import mixed_grads, mixed_spec
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", HYBRIDAGENT_B200_COMM=mode.split("_")[0])
+    if mode == "p2p_rounds":
+        env["HYBRIDAGENT_B200_RECV_BYTES"] = "4096"
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29735",
+           os.path.join(HERE, "world_worker.py"), "mixed", str(tmp_path)]
+    proc = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    res = [pickle.load(open(tmp_path / f"rank{r}.pkl", "rb")) for r in range(2)]
+    assert res[0]["mode"] == res[1]["mode"] == mode.split("_")[0]
+    assert res[0]["norms"] == res[1]["norms"]
+    spec = mixed_spec()
+    rng = np.random.default_rng(3)
+    init = [Z.narrow((rng.standard_normal(int(np.prod(s))) * 0.02).astype(np.float32), d) for s, d in spec]
+    ora = Z.OracleZeroOne(init, [d for _, d in spec], [1e-3] * 4 + [3e-4] * 4, world=2, weight_decay=0.05)
+    assert ora.owner == res[0]["owner"]
+    for step in range(3):
+        ora.reduce_grads([mixed_grads(step, r) for r in range(2)])
+        mine = Z.norm_from_sumsq(ora.sumsq())
+        assert Z.isclose_norm(res[0]["norms"][step], mine, 1e-6), (step, res[0]["norms"][step], mine)
+        ora.clip_grad_norm(1.0, norm=res[0]["norms"][step])
+        ora.step()
+    for i, (_, d) in enumerate(spec):
+        assert np.array_equal(res[0]["params"][i].view(np.uint8), res[1]["params"][i].view(np.uint8)), i
+        assert_bits_equal(res[0]["params"][i], ora.params[i], f"param[{i}]")
+        master, m, v, steps = res[ora.owner[i]]["state"][i]
+        om, oea, oeas, osteps = ora.tensor_state(i)
+        assert steps == osteps
+        assert_bits_equal(master, om, f"master[{i}]")
+        assert_bits_equal(m, oea, f"exp_avg[{i}]")
+        assert_bits_equal(v, oeas, f"exp_avg_sq[{i}]")

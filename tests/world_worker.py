@@ -93,6 +93,65 @@ def peer_delay(out_dir: str) -> None:
     os._exit(0)  # the communicator is aborted: skip collective teardown
 
 
+def mixed(out_dir: str) -> None:
+    """bf16, fp32 and fp16 parameters in one optimizer at world size W (three dtype classes,
+    each with its own exchange rounds), three steps; writes this rank's results."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from helpers import Z, to_numpy, to_torch
+    from hybridagent_b200 import ZeroOneAdamW
+
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    spec = mixed_spec()
+    rng = np.random.default_rng(3)
+    init = [Z.narrow((rng.standard_normal(int(np.prod(s))) * 0.02).astype(np.float32), d) for s, d in spec]
+    params = [torch.nn.Parameter(to_torch(b, d, s, dev)) for b, (s, d) in zip(init, spec)]
+    opt = ZeroOneAdamW([{"params": params[:4], "lr": 1e-3}, {"params": params[4:], "lr": 3e-4}], rank=rank,
+                       world_size=world, weight_decay=0.05)
+    norms = []
+    for step in range(3):
+        opt.zero_grad(set_to_none=True)
+        for p, g, (s, d) in zip(params, mixed_grads(step, rank), spec):
+            p.grad = None if g is None else to_torch(g, d, s, dev)
+        opt.all_reduce_grads()
+        norms.append(opt.clip_grad_norm(1.0))
+        opt.step()
+    torch.cuda.synchronize()
+    result = {"rank": rank, "norms": norms, "owner": opt.owner, "mode": opt.comm_mode,
+              "params": [to_numpy(p.data, d) for p, (_, d) in zip(params, spec)],
+              "state": {i: (to_numpy(opt.master[i], 0), to_numpy(opt.exp_avg[i], 0), to_numpy(opt.exp_avg_sq[i], 0),
+                            opt.param_steps[i]) for i in opt.param_steps}}
+    with open(os.path.join(out_dir, f"rank{rank}.pkl"), "wb") as f:
+        pickle.dump(result, f)
+    dist.barrier()
+    opt.close()
+    dist.destroy_process_group()
+
+
+def mixed_spec():
+    from helpers import Z
+    return [((64, 96), Z.BF16), ((33,), Z.F32), ((1000,), Z.BF16), ((48, 16), Z.F32), ((40, 24), Z.F16),
+            ((4097,), Z.BF16), ((7,), Z.F16), ((256, 64), Z.F32)]
+
+
+def mixed_grads(step, rank):
+    """Rank-dependent gradients; tensor 2 is absent on rank 1 at step 1."""
+    import numpy as np
+
+    from helpers import Z
+    rng = np.random.default_rng([11, step, rank])
+    out = []
+    for k, (s, d) in enumerate(mixed_spec()):
+        g = Z.narrow((rng.standard_normal(int(np.prod(s))) * 0.05).astype(np.float32), d)
+        out.append(None if (k == 2 and step == 1 and rank == 1) else g)
+    return out
+
+
 def main(name: str, out_dir: str) -> None:
     import torch
     import torch.distributed as dist
@@ -149,5 +208,7 @@ def main(name: str, out_dir: str) -> None:
 if __name__ == "__main__":
     if sys.argv[1] == "peer_delay":
         peer_delay(sys.argv[2])
+    elif sys.argv[1] == "mixed":
+        mixed(sys.argv[2])
     else:
         main(sys.argv[1], sys.argv[2])
