@@ -23,6 +23,13 @@ Printed (rank 0, one JSON line):
                bounded sample of the same parameter set;
   clocks       nvidia-smi samples taken during the timed region.
 ``--impl reference`` times only that CPU implementation (rank 0; other ranks exit).
+
+``--landing`` (N > 1) measures gradient landing instead and prints its own JSON line: a
+synthetic forward + backward whose weight gradients are GEMMs over ``--tokens`` tokens
+(one ``linear`` per matrix, a dot product per vector) followed by the optimizer sequence,
+with the early pushes off and on (same optimizer, receive window sized for two rounds so
+the whole exchange can start during backward); per variant the forward + backward time,
+the optimizer time left after backward, and their sum, max over ranks.
 """
 from __future__ import annotations
 
@@ -61,6 +68,10 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-params", type=int, default=200_000_000)
     ap.add_argument("--max-params", type=int, default=0, help="truncate the parameter set (smoke / profiling)")
+    ap.add_argument("--landing", action="store_true", help="measure gradient landing (N > 1)")
+    ap.add_argument("--tokens", type=int, default=2048, help="tokens of the --landing synthetic backward")
+    ap.add_argument("--land-ctas", default="0,64", help="--landing: comma-separated CTA caps of the early "
+                    "pushes to measure (0: copy engines)")
     return ap.parse_args()
 
 
@@ -405,10 +416,105 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def run_landing(args) -> None:
+    """Gradient landing: forward + backward + optimizer step, early pushes off vs on."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    from hybridagent_b200 import ZeroOneAdamW, workloads
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus or world < 2:
+        raise SystemExit("--landing needs --gpus N > 1 under torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    shapes = workloads.WORKLOADS[args.workload]()
+    if args.max_params:
+        shapes = workloads.truncated(shapes, args.max_params)
+    n_params = sum(math.prod(s) for s in shapes)
+    # a receive window of two rounds: every piece may be pushed while its gradient lands
+    os.environ["HYBRIDAGENT_B200_RECV_BYTES"] = str(2 * n_params + (256 << 20))
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    params = [torch.nn.Parameter((torch.randn(s, device=dev, generator=gen) * 0.02).to(torch.bfloat16))
+              for s in shapes]
+    opt = ZeroOneAdamW([{"params": params, "lr": 1e-6}], rank=rank, world_size=world, weight_decay=0.01,
+                       land_grads=True)
+    gx = torch.Generator(device=dev).manual_seed(777 + rank)
+    T = args.tokens
+    dims_in = sorted({s[1] for s in shapes if len(s) == 2})
+    dims_out = max(s[0] for s in shapes if len(s) == 2)
+    x = {d: (torch.randn(T, d, device=dev, generator=gx) * 0.02).to(torch.bfloat16) for d in dims_in}
+    r = (torch.randn(T, dims_out, device=dev, generator=gx) * 1e-3).to(torch.bfloat16)
+    v = {s[0]: (torch.randn(s[0], device=dev, generator=gx) * 1e-3).to(torch.bfloat16)
+         for s in shapes if len(s) == 1}
+
+    def fwd_bwd():
+        terms = []
+        for p in params:
+            if p.dim() == 2:
+                terms.append((F.linear(x[p.shape[1]], p) * r[:, :p.shape[0]]).sum())
+            else:
+                terms.append((p * v[p.shape[0]]).sum())
+        torch.autograd.backward(terms)
+
+    def one(ev):
+        opt.zero_grad(set_to_none=True)
+        ev[0].record()
+        fwd_bwd()
+        ev[1].record()
+        opt.all_reduce_grads()
+        opt.clip_grad_norm(1.0)
+        opt.step()
+        ev[2].record()
+
+    out = {}
+    caps = [int(x) for x in args.land_ctas.split(",")]
+    for variant in ["off"] + [f"on_ctas{n}" for n in caps]:
+        opt.landing_enabled = variant != "off"
+        if opt.landing_enabled:
+            opt.land_ctas = int(variant[len("on_ctas"):])
+        launches0 = opt.land_launches
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+        for _ in range(max(args.warmup, 3)):
+            one([torch.cuda.Event(enable_timing=True) for _ in range(3)])
+        dist.barrier()
+        torch.cuda.synchronize()
+        for ev in evs:
+            one(ev)
+        torch.cuda.synchronize()
+        fb = sum(e[0].elapsed_time(e[1]) for e in evs) / len(evs)
+        st = sum(e[1].elapsed_time(e[2]) for e in evs) / len(evs)
+        t = torch.tensor([fb, st, fb + st], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out[variant] = {"fwd_bwd_ms": round(float(t[0]), 3), "step_after_backward_ms": round(float(t[1]), 3),
+                        "total_ms": round(float(t[2]), 3),
+                        "early_push_calls_per_step": (opt.land_launches - launches0) // (len(evs) + max(args.warmup, 3))}
+    best = min((k for k in out if k != "off"), key=lambda k: out[k]["total_ms"])
+    if rank == 0:
+        line = {"metric": "fwd_bwd_plus_step_ms", "value": out[best]["total_ms"], "unit": "ms", "n_gpus": world,
+                "steps": args.steps, "warmup": max(args.warmup, 3), "higher_is_better": False, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": args.workload, "params": n_params, "tensors": len(shapes), "tokens": T,
+                           "recv_window_bytes": int(os.environ["HYBRIDAGENT_B200_RECV_BYTES"]),
+                           "comm_mode": opt.comm_mode, "parallelism": f"zero1-dp{world}"},
+                "landing": out, "best": best,
+                "saved_ms": round(out["off"]["total_ms"] - out[best]["total_ms"], 3)}
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    opt.close()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.landing:
+        run_landing(args)
     else:
         run_ours(args)
 

@@ -66,6 +66,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "ha_grad_sumsq_noalloc": ([_vp, _vp, _i64, _i64, ctypes.c_int, _vp, _vp], ctypes.c_int),
     "ha_scale_grads": ([_vp, _vp, _i64, _i64, ctypes.c_int, _f32, _vp], ctypes.c_int),
     "ha_gather": ([_vp, _vp, _i64, _i64, ctypes.c_int, _vp], ctypes.c_int),
+    "ha_gather_capped": ([_vp, _vp, _i64, _i64, ctypes.c_int, ctypes.c_int32, _vp], ctypes.c_int),
+    "ha_copy_async": ([_vp, _i64, ctypes.c_int, _vp], ctypes.c_int),
     "ha_malloc": ([_sz, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "ha_free": ([_vp], ctypes.c_int),
     "ha_memset": ([_vp, ctypes.c_int, _sz, _vp], ctypes.c_int),

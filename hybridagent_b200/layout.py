@@ -186,6 +186,63 @@ def exchange_pieces(cls: DtypeClass, owner: list[int], numels: list[int], round_
     return Pieces(*arr, n_rounds=n_rounds, round_elems=S)
 
 
+LAND_ROUNDS = 2  # exchange rounds whose window halves are free between one update and the next exchange
+
+
+def landing_pieces(pc: Pieces, n_entries: int) -> list[np.ndarray]:
+    """Per table entry, the indices of its pieces that may be pushed while the gradient is
+    still landing during backward: the pieces of rounds 0 and 1.  Between the barrier that
+    ends an update (after every owner's sums of the previous exchange) and the first barrier
+    of the next exchange nobody reads either half of any receive window, so those pieces can
+    be stored early; later rounds reuse a half and must wait for the exchange's barriers."""
+    sel = np.nonzero((pc.round < LAND_ROUNDS) & (pc.tensor >= 0))[0]
+    order = sel[np.argsort(pc.tensor[sel], kind="stable")]
+    bounds = np.searchsorted(pc.tensor[order], np.arange(n_entries + 1))
+    return [order[bounds[k]:bounds[k + 1]] for k in range(n_entries)]
+
+
+def piece_destinations(pc: Pieces, recv_bases: list[int], rank: int, world: int, elem_bytes: int) -> np.ndarray:
+    """Address of every piece in its owner's receive window: half ``round % 2``, region
+    ``rank`` (windows of 2 x world regions of ``round_elems`` elements)."""
+    bases = np.asarray(recv_bases, dtype=np.uint64)
+    S = pc.round_elems
+    return bases[pc.owner] + (((pc.round % 2) * world * S + rank * S + pc.dst_off) * elem_bytes).astype(np.uint64)
+
+
+def piece_sources(pc: Pieces, entry_ptrs: np.ndarray, elem_bytes: int, dst: np.ndarray | None = None,
+                  landed: np.ndarray | None = None) -> np.ndarray:
+    """Source address of every piece: its gradient's address (``entry_ptrs`` per table
+    entry, 0 for a tensor without one: zero-fill) plus the piece's offset; gaps zero-fill.
+    The early pieces (rounds < LAND_ROUNDS) of entries marked in ``landed`` were pushed
+    during backward and get src == dst, which the gather kernel skips."""
+    pt = np.where(pc.tensor >= 0, np.asarray(entry_ptrs, dtype=np.uint64)[np.maximum(pc.tensor, 0)], 0)
+    pt = pt.astype(np.uint64)
+    src = np.where(pt != 0, pt + (pc.src_off * elem_bytes).astype(np.uint64), 0).astype(np.uint64)
+    if landed is not None:
+        skip = (pc.round < LAND_ROUNDS) & (pc.tensor >= 0) & np.asarray(landed, dtype=bool)[np.maximum(pc.tensor, 0)]
+        src[skip] = dst[skip]
+    return src
+
+
+def landing_batch(src: np.ndarray, dst: np.ndarray, count: np.ndarray, chunk_elems: int) -> tuple[np.ndarray, np.ndarray]:
+    """ha_copy entries (piece j: ``count[j]`` elements from address ``src[j]`` to ``dst[j]``)
+    and the ha_chunk list that covers them, for one early push of landed gradients."""
+    n = len(src)
+    copies = np.zeros(n, dtype=_lib.COPY_DTYPE)
+    copies["src"] = src
+    copies["dst"] = dst
+    copies["numel"] = count
+    per = (np.asarray(count, dtype=np.int64) + chunk_elems - 1) // chunk_elems
+    total = int(per.sum())
+    chunks = np.zeros(total, dtype=_lib.CHUNK_DTYPE)
+    if total:
+        chunks["tensor"] = np.repeat(np.arange(n, dtype=np.uint32), per)
+        chunks["index"] = np.arange(total, dtype=np.int64) - np.repeat(np.cumsum(per) - per, per)
+        _lib.call("ha_check_chunks", n, _lib.np_ptr(np.ascontiguousarray(count, dtype=np.int64)), _lib.np_ptr(chunks),
+                  total, chunk_elems)
+    return copies, chunks
+
+
 def interleaved_chunks(entries: np.ndarray, entry_owner: np.ndarray, entry_numel: np.ndarray, rank: int, world: int,
                        chunk_elems: int) -> np.ndarray:
     """ha_chunk list over the given table entries, one chunk per owner in turn (starting

@@ -50,6 +50,10 @@ Deliberate differences (documented surface):
 * At world_size > 1 in p2p mode the norm's square sums come out of ``all_reduce_grads``;
   ``clip_grad_norm`` recomputes them if an owned ``p.grad`` was replaced in between, but
   not if one was modified in place (the reference's trainer does neither).
+* ``land_grads=True`` (new, opt-in, p2p mode) pushes the first two exchange rounds of each
+  gradient to its owner while backward is still running (post-accumulate-grad hooks); results
+  are unchanged, but a gradient modified in place after its last landing and before
+  ``all_reduce_grads`` is not sent again (a replaced one is).
 * ``use_8bit=True`` (bitsandbytes PagedAdamW8bit, optimizer.py:76-86) is not provided.
 * ``state_dict`` / ``load_state_dict`` are new (the reference has neither).
 """
@@ -57,6 +61,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import weakref
 from collections.abc import MutableMapping
 
 import numpy as np
@@ -217,11 +222,10 @@ class _Class:
             base = self.own_grad
             own0 = 0
             self.move = _Table(len(pc.count), _lib.COPY_DTYPE, dev)
-            bases = np.asarray(recv_bases, dtype=np.uint64)
-            dst = bases[pc.owner] + (((pc.round % 2) * W * S + r * S + pc.dst_off) * esz).astype(np.uint64)
+            dst = layout.piece_destinations(pc, recv_bases, r, W, esz)
+            self.piece_dst = dst
             self.move.np["dst"][:len(dst)] = dst
             self.move.np["numel"][:len(dst)] = pc.count
-            self.piece_tensor = pc.tensor
             self.piece_src_bytes = (pc.src_off * esz).astype(np.uint64)
             self.round_chunks = []
             for k in range(pc.n_rounds):
@@ -232,6 +236,9 @@ class _Class:
                 self.round_chunks.append((torch.from_numpy(tab.view(np.uint8).copy()).to(dev) if len(tab) else None,
                                           len(tab)))
             self.own_counts = pc.own_counts(cls, r)
+            # gradient landing: the pieces that may be pushed during backward (rounds 0 and 1)
+            self.land_pieces = layout.landing_pieces(pc, len(cls.indices))
+            self.land_mask = (pc.round < layout.LAND_ROUNDS) & (pc.tensor >= 0)
             n_part = max(-(-S // HA_SUM_REGIONS_CHUNK), 1)
             self.region_partials = [torch.empty(n_part, dtype=torch.float64, device=dev) for _ in range(2)]
             self.peers = _lib.Peers()
@@ -266,10 +273,12 @@ class ZeroOneAdamW:
     """ZeRO-1 AdamW over CUDA parameters (drop-in for hybrid_rl.optimizer.ZeroOneAdamW)."""
 
     def __init__(self, param_groups, *, rank: int, world_size: int, betas=(0.9, 0.999), eps: float = 1e-8,
-                 weight_decay: float = 0.0, use_8bit: bool = False, comm_timeout_s: float | None = None):
+                 weight_decay: float = 0.0, use_8bit: bool = False, comm_timeout_s: float | None = None,
+                 land_grads: bool = False):
         # argument handling and errors as optimizer.py:24-44; comm_timeout_s (world > 1): seconds a
         # collective may wait for the other ranks before the communicator is aborted and the call
-        # raises CommFailure (default HYBRIDAGENT_B200_COMM_TIMEOUT_S or 1800)
+        # raises CommFailure (default HYBRIDAGENT_B200_COMM_TIMEOUT_S or 1800); land_grads (world > 1,
+        # p2p mode): push gradients to their owners while backward is still running
         self.rank = int(rank)
         self.world = int(world_size)
         self.betas = tuple(float(value) for value in betas)
@@ -331,8 +340,10 @@ class ZeroOneAdamW:
             # pinned landing buffers of the host reads (deadline-aware waits at world > 1)
             self._norm_host = torch.zeros(len(self._classes), dtype=torch.float64, pin_memory=True)
             if self.world > 1:
+                # this rank's mask (uploaded asynchronously: the next call rewrites it only after
+                # reading the all-reduce that follows the upload) and the all-reduced mask
+                self._used_local = torch.zeros(len(self.params), dtype=torch.uint8, pin_memory=True)
                 self._used_host = torch.zeros(len(self.params), dtype=torch.uint8, pin_memory=True)
-            if self.world > 1:
                 self._setup_world()
             torch.cuda.current_stream().synchronize()
         self._pending_clip: float | None = None
@@ -340,6 +351,12 @@ class ZeroOneAdamW:
         self._grad_cache: dict[int, tuple] = {}
         self.timer = None  # optional phase timer: .begin(name) / .end(name) around kernel launches
         self.launches = 0  # kernels of libhybridagent_b200 launched so far
+        self.landing_enabled = False  # gradient landing active (toggle it off for non-final backward passes)
+        self.land_launches = 0  # early pushes launched from the landing hooks
+        self._land_hooks: list = []
+        self._landed: dict[int, torch.Tensor] = {}
+        if land_grads and self.comm_mode == "p2p":
+            self._setup_landing()
 
     def _setup_world(self) -> None:
         """Owners' parameter values to every rank (the reference's broadcast), then the
@@ -481,12 +498,149 @@ class ZeroOneAdamW:
                       self.betas[0], self.betas[1], self.weight_decay, _lib.np_ptr(tab))
         c.table.upload()
 
+    # ---------------------------------------------------------------- gradient landing
+    def _setup_landing(self) -> None:
+        """Gradient landing (p2p mode): a post-accumulate-grad hook on every parameter
+        (the point where the reference's trainer hands the gradient over, train.py:268)
+        pushes the pieces of the new gradient that belong to exchange rounds 0 and 1 to their
+        owners' receive windows while backward is still running, on a separate stream, in
+        buckets of HYBRIDAGENT_B200_LAND_BUCKET_BYTES (default 256 MiB) and at the end of each
+        backward pass.  ``all_reduce_grads`` then pushes only the rest.  A gradient that lands
+        again (a later backward of the same step) is pushed again; the last push wins.
+
+        The pushes go to the copy engines (``land_ctas`` 0, the default), which take no SM from
+        backward's kernels; HYBRIDAGENT_B200_LAND_CTAS=N > 0 runs them as a kernel of N CTAs
+        walking the chunk list instead (measured on B200 at W=2: the copy engines cost backward
+        4.4 ms for 16.4 GB moved, a 64-CTA kernel 12.9 ms, 8-32 CTAs too slow to finish within
+        backward).  The copy tables of the kernel pushes go through a pinned arena (host) and its
+        device twin, appended per push and rewound once the exchange has consumed them."""
+        self._land_stream = torch.cuda.Stream(device=self.device)
+        self._entry_of = {}
+        n_pieces = n_chunks = 0
+        for ci, c in enumerate(self._classes):
+            for k, i in enumerate(c.layout.indices):
+                self._entry_of[i] = (ci, k)
+            n_pieces += int(c.land_mask.sum())
+            n_chunks += int(((c.pieces.count[c.land_mask] + HA_ADAMW_CHUNK - 1) // HA_ADAMW_CHUNK).sum())
+        # room for two landings of every gradient in one step before the arena is rewound
+        self._land_cap = (max(2 * n_pieces, 1), max(2 * n_chunks, 1))
+        csz, hsz = _lib.COPY_DTYPE.itemsize, _lib.CHUNK_DTYPE.itemsize
+        self._land_copies = (torch.empty(self._land_cap[0] * csz, dtype=torch.uint8, pin_memory=True),
+                             torch.empty(self._land_cap[0] * csz, dtype=torch.uint8, device=self.device))
+        self._land_chunks = (torch.empty(self._land_cap[1] * hsz, dtype=torch.uint8, pin_memory=True),
+                             torch.empty(self._land_cap[1] * hsz, dtype=torch.uint8, device=self.device))
+        self._land_cursor = [0, 0]
+        self._land_pending: list = []  # (class, entry, gradient, stream it was accumulated on)
+        self._land_pending_bytes = 0
+        self._land_bucket = int(os.environ.get("HYBRIDAGENT_B200_LAND_BUCKET_BYTES", str(256 << 20)))
+        # 0: early pushes on the copy engines (no SM taken from backward); N > 0: a pushing
+        # kernel on N CTAs (remote stores move ~6 GB/s per CTA, so it must take many SMs)
+        self.land_ctas = int(os.environ.get("HYBRIDAGENT_B200_LAND_CTAS", "0"))
+        self._land_ok = True         # no exchange of this optimizer is between its pushes and its update
+        self._land_waited = False    # the landing stream already waits for the last update's barrier
+        self._window_free = None     # event after that barrier
+        self._land_callback = False  # an end-of-backward flush is queued
+        me = weakref.ref(self)
+
+        def hook(i):
+            def on_landed(p):
+                opt = me()
+                if opt is not None:
+                    opt._on_landed(i, p)
+            return on_landed
+
+        self._land_hooks = [p.register_post_accumulate_grad_hook(hook(i)) for i, p in enumerate(self.params)]
+        self.landing_enabled = True
+
+    def _on_landed(self, i: int, p: torch.Tensor) -> None:
+        """Post-accumulate-grad hook of parameter i (runs on the autograd engine's thread)."""
+        if not (self.landing_enabled and self._land_ok):
+            return
+        ci, k = self._entry_of[i]
+        c = self._classes[ci]
+        g = p.grad
+        if (g is None or g.dtype != c.dtype or g.device != self.device or g.numel() != self._numels[i]
+                or not g.is_contiguous() or not len(c.land_pieces[k])):
+            self._landed.pop(i, None)  # all_reduce_grads pushes it
+            return
+        self._landed[i] = g
+        self._land_pending.append((ci, k, g, torch.cuda.current_stream(self.device)))
+        self._land_pending_bytes += g.numel() * g.element_size()
+        if not self._land_callback:
+            self._land_callback = True
+            torch.autograd.Variable._execution_engine.queue_callback(self._land_end_of_backward)
+        if self._land_pending_bytes >= self._land_bucket:
+            self._land_flush()
+
+    def _land_end_of_backward(self) -> None:
+        self._land_callback = False
+        self._land_flush()
+
+    def _land_flush(self) -> None:
+        """Pushes the pending landed gradients' early pieces on the landing stream."""
+        pending, self._land_pending, self._land_pending_bytes = self._land_pending, [], 0
+        if not pending:
+            return
+        land = self._land_stream
+        with torch.cuda.device(self.device):
+            for st in {st.cuda_stream: st for *_, st in pending}.values():
+                land.wait_stream(st)  # the gradients are complete
+            if not self._land_waited:
+                if self._window_free is not None:
+                    land.wait_event(self._window_free)  # every owner has read the previous exchange
+                self._land_waited = True
+            by_class: dict[int, list] = {}
+            for ci, k, g, _ in pending:
+                by_class.setdefault(ci, []).append((k, g))
+            csz, hsz = _lib.COPY_DTYPE.itemsize, _lib.CHUNK_DTYPE.itemsize
+            for ci, items in by_class.items():
+                c = self._classes[ci]
+                idx = np.concatenate([c.land_pieces[k] for k, _ in items])
+                base = np.concatenate([np.full(len(c.land_pieces[k]), g.data_ptr(), dtype=np.uint64)
+                                       for k, g in items])
+                copies, chunks = layout.landing_batch(base + c.piece_src_bytes[idx], c.piece_dst[idx],
+                                                      c.pieces.count[idx], HA_ADAMW_CHUNK)
+                if self.land_ctas == 0:  # copy engines: the host table is read by the calls themselves
+                    _lib.call("ha_copy_async", _lib.np_ptr(copies), len(copies), c.packed_param.element_size(),
+                              land.cuda_stream)
+                    self.land_launches += 1
+                    continue
+                a, b = self._land_cursor
+                if a + len(copies) > self._land_cap[0] or b + len(chunks) > self._land_cap[1]:
+                    land.synchronize()  # every earlier upload has been consumed: rewind the arena
+                    a = b = 0
+                hc, dc = self._land_copies
+                hk, dk = self._land_chunks
+                hc.numpy()[a * csz:(a + len(copies)) * csz] = copies.view(np.uint8)
+                hk.numpy()[b * hsz:(b + len(chunks)) * hsz] = chunks.view(np.uint8)
+                with torch.cuda.stream(land):
+                    dc[a * csz:(a + len(copies)) * csz].copy_(hc[a * csz:(a + len(copies)) * csz], non_blocking=True)
+                    dk[b * hsz:(b + len(chunks)) * hsz].copy_(hk[b * hsz:(b + len(chunks)) * hsz], non_blocking=True)
+                _lib.call("ha_gather_capped", dc.data_ptr() + a * csz, dk.data_ptr() + b * hsz, len(chunks),
+                          HA_ADAMW_CHUNK, c.packed_param.element_size(), self.land_ctas, land.cuda_stream)
+                self.launches += 1
+                self.land_launches += 1
+                self._land_cursor = [a + len(copies), b + len(chunks)]
+            for _, _, g, _ in pending:
+                g.record_stream(land)  # the allocator keeps it until the push has read it
+
+    def _land_join(self) -> None:
+        """Start of an exchange: flushes what is pending and orders the current stream after
+        every early push (the arena is rewound once the next host read has waited for it)."""
+        self._land_flush()
+        self._land_callback = False
+        torch.cuda.current_stream(self.device).wait_stream(self._land_stream)
+
     # ---------------------------------------------------------------- reference surface
     def zero_grad(self, set_to_none: bool = True) -> None:
         """optimizer.py:88-93."""
         self._pending_clip = None
         self._fused_sumsq = None
         self._grad_cache = {}
+        self._landed = {}  # what was pushed early no longer matches the gradients
+        if self._land_hooks:  # (a backward that raised may have left both behind)
+            self._land_pending, self._land_pending_bytes = [], 0
+            self._land_callback = False
         for parameter in self.params:
             if set_to_none:
                 parameter.grad = None
@@ -506,7 +660,11 @@ class ZeroOneAdamW:
             # synchronised, overlapping the GPU's earlier work (it dominates with ~10^4 tensors)
             keep = []  # gradients that must stay alive until the move kernel has read them
             p2p = self.comm_mode == "p2p"
-            local = np.zeros(len(self.params), dtype=np.uint8)
+            landed = self._landed
+            if self._land_hooks:
+                self._land_join()
+            local = self._used_local.numpy()
+            local[:] = 0
             class_ptrs = []
             for c in self._classes:
                 ptrs = np.zeros(len(c.layout.indices), dtype=np.uint64)
@@ -527,16 +685,27 @@ class ZeroOneAdamW:
                     keep.append(g)
                     ptrs[k] = g.data_ptr()
                 class_ptrs.append(ptrs)
-            self._used_dev.copy_(torch.from_numpy(local), non_blocking=False)
+            self._used_dev.copy_(self._used_local, non_blocking=True)  # no host wait: a peer may be missing
             self._comm.all_reduce_max(self._used_dev, HA_U8)
             # a rank that stopped answering ends here (CommFailure), before any peer store
             used = self._comm.read(self._used_dev, self._used_host, "all-reduce(max) of the used mask")
             used = used.numpy().astype(bool)
-            for c, ptrs in zip(self._classes, class_ptrs):
+            if self._land_hooks:  # the early pushes have all completed: rewind their arena
+                self._land_cursor = [0, 0]
+                self._land_waited = False
+                self._land_ok = False  # until the update's barrier frees the windows again
+                self._landed = {}
+            for ci, (c, ptrs) in enumerate(zip(self._classes, class_ptrs)):
                 ptrs[~used[np.asarray(c.layout.indices)]] = 0  # unused everywhere: zeros (optimizer.py:111-114)
-                if p2p:  # each piece reads its part of its tensor's gradient (0: zero-fill; -1: a gap)
-                    pt = np.where(c.piece_tensor >= 0, ptrs[np.maximum(c.piece_tensor, 0)], 0).astype(np.uint64)
-                    c.move.np["src"][:len(pt)] = np.where(pt != 0, pt + c.piece_src_bytes, 0)
+                if p2p:  # each piece reads its part of its tensor's gradient (0: zero-fill; gaps: zeros)
+                    done = None
+                    if landed:  # pieces pushed while their gradient landed, gradient unchanged: skipped
+                        done = np.zeros(len(c.layout.indices), dtype=bool)
+                        for i, g in landed.items():
+                            if self._entry_of[i][0] == ci and self.params[i].grad is g:
+                                done[self._entry_of[i][1]] = True
+                    src = layout.piece_sources(c.pieces, ptrs, c.packed_param.element_size(), c.piece_dst, done)
+                    c.move.np["src"][:len(src)] = src
                 else:  # equal to dst when the gradient already lives in its slot
                     c.move.np["src"][:len(ptrs)] = ptrs
                 c.move.upload()
@@ -670,6 +839,10 @@ class ZeroOneAdamW:
                 self._phase("barrier", True)
                 self._barrier()  # peers use their parameters only after every rank's stores landed
                 self._phase("barrier", False)
+                if self._land_hooks:  # every owner has read its windows: early pushes may start
+                    self._window_free = torch.cuda.Event()
+                    self._window_free.record()
+                    self._land_ok = True
             elif self.world > 1:
                 self._phase("all_gather", True)
                 for c in self._classes:
@@ -733,6 +906,10 @@ class ZeroOneAdamW:
     def close(self) -> None:
         """Releases the peer mappings and the NCCL communicator (world_size > 1).  Call it on
         every rank after the last step."""
+        for h in getattr(self, "_land_hooks", []):
+            h.remove()
+        self._land_hooks = []
+        self.landing_enabled = False
         if self._peer_map is not None:
             torch.cuda.current_stream(self.device).synchronize()
             self._peer_map.close()

@@ -172,6 +172,17 @@ int ha_scale_grads(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t
 int ha_gather(const ha_copy* d_copies, const ha_chunk* d_chunks, int64_t n_chunks, int64_t chunk_elems,
               int elem_bytes, void* stream);
 
+/* ha_gather on at most max_ctas (> 0) CTAs that walk the chunk list with the grid's stride:
+ * the early gradient pushes made while backward still runs (gradient landing at
+ * hybrid_rl/train.py:268's loss.backward()) occupy a few SMs instead of all of them. */
+int ha_gather_capped(const ha_copy* d_copies, const ha_chunk* d_chunks, int64_t n_chunks, int64_t chunk_elems,
+                     int elem_bytes, int32_t max_ctas, void* stream);
+
+/* The same copies from a HOST table, issued to the copy engines: one cudaMemcpyAsync
+ * (src != 0) or cudaMemsetAsync (src == 0, zero-fill) per entry on `stream`; entries with
+ * src == dst are skipped.  Uses no SM. */
+int ha_copy_async(const ha_copy* h_copies, int64_t n, int elem_bytes, void* stream);
+
 
 /* ------------------------------------------------------------------ peer-to-peer (NVLink / NVSwitch) */
 

@@ -98,6 +98,18 @@ def test_kernel_entry_points_validate_arguments_without_a_gpu():
     _lib.call("ha_adamw_step", None, None, 0, _lib.HA_ADAMW_CHUNK, _lib.HA_BF16, _lib.HA_BF16, ctypes.byref(sc), None)
     with pytest.raises(_lib.HAError, match="elem_bytes"):
         _lib.call("ha_gather", None, None, 1, 16384, 3, None)
+    with pytest.raises(_lib.HAError, match="max_ctas"):
+        _lib.call("ha_gather_capped", None, None, 1, 16384, 2, 0, None)
+    _lib.call("ha_gather_capped", None, None, 0, 16384, 2, 8, None)  # nothing to copy: no launch
+    with pytest.raises(_lib.HAError, match="elem_bytes"):
+        _lib.call("ha_copy_async", None, 0, 8, None)
+    bad = np.zeros(1, dtype=_lib.COPY_DTYPE)  # dst 0
+    with pytest.raises(_lib.HAError, match="entry 0"):
+        _lib.call("ha_copy_async", _lib.np_ptr(bad), 1, 2, None)
+    same = np.zeros(1, dtype=_lib.COPY_DTYPE)
+    same["src"] = same["dst"] = 4096
+    same["numel"] = 10
+    _lib.call("ha_copy_async", _lib.np_ptr(same), 1, 2, None)  # src == dst: skipped, no CUDA call
     with pytest.raises(_lib.HAError):
         _lib.call("ha_grad_sumsq", None, None, 5, _lib.HA_SUMSQ_CHUNK, _lib.HA_BF16, None, None, None)
     with pytest.raises(_lib.HAError):

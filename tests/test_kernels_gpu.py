@@ -205,8 +205,11 @@ def test_scale_grads(code):
         assert_bits_equal(to_numpy(ts.grad[k], code), want, f"grad[{k}]")
 
 
+@pytest.mark.parametrize("how", ["per_chunk", "capped1", "capped3", "capped64", "copy_engine"])
 @pytest.mark.parametrize("elem", [2, 4])
-def test_gather(elem):
+def test_gather(elem, how):
+    """ha_gather (one CTA per chunk), ha_gather_capped (a grid of 1, 3 or 64 CTAs walking the
+    chunk list) and ha_copy_async (copy engines) make the same copies and zero-fills."""
     import torch
     dt = torch.bfloat16 if elem == 2 else torch.float32
     sizes = [5, 16384, 16385, 40000, 1, 0, 333]
@@ -223,7 +226,13 @@ def test_gather(elem):
         tab[k]["numel"] = n
     chunks = layout.chunk_table(sizes, 16384)
     dtab, dchunks = _dev_bytes(tab), _dev_bytes(chunks)  # device tables must outlive the launch
-    _lib.call("ha_gather", dtab.data_ptr(), dchunks.data_ptr(), len(chunks), 16384, elem, _stream())
+    if how == "per_chunk":
+        _lib.call("ha_gather", dtab.data_ptr(), dchunks.data_ptr(), len(chunks), 16384, elem, _stream())
+    elif how == "copy_engine":
+        _lib.call("ha_copy_async", _lib.np_ptr(tab), len(tab), elem, _stream())
+    else:
+        _lib.call("ha_gather_capped", dtab.data_ptr(), dchunks.data_ptr(), len(chunks), 16384, elem,
+                  int(how[len("capped"):]), _stream())
     torch.cuda.synchronize()
     for k, n in enumerate(sizes):
         got = dst[offs[k]:offs[k] + n]

@@ -103,3 +103,91 @@ def test_round_elems_for_budget():
     S = layout.round_elems_for(cls, 8, 2, 2 << 30)
     assert S % layout.ALIGN == 0 and 2 * 8 * S * 2 <= 2 << 30
     assert layout.round_elems_for(cls, 8, 2, 1 << 60) == cls.seg_len
+
+
+def _emulate_gather(memory, copies, chunks, chunk_elems, esz):
+    """ha_gather on simulated memory (``memory``: base >> 40 -> numpy array; addresses are
+    base << 40 plus a byte offset): per chunk, src == dst skips, src == 0 zero-fills."""
+    import numpy as np
+    for t, j in zip(chunks["tensor"], chunks["index"]):
+        c = copies[int(t)]
+        src, dst, n = int(c["src"]), int(c["dst"]), int(c["numel"])
+        lo, hi = int(j) * chunk_elems, min(n, (int(j) + 1) * chunk_elems)
+        assert 0 <= lo < hi
+        if src == dst:
+            continue
+        d = memory[dst >> 40]
+        do = (dst & ((1 << 40) - 1)) // esz
+        if src == 0:
+            d[do + lo:do + hi] = 0
+        else:
+            s = memory[src >> 40]
+            so = (src & ((1 << 40) - 1)) // esz
+            d[do + lo:do + hi] = s[so + lo:so + hi]
+    return np
+
+
+@pytest.mark.parametrize("world,S", [(2, 64 * 20), (3, 64 * 7), (2, 64 * 100_000)])
+def test_landing_then_residual_equals_plain_exchange(world, S):
+    """Early pushes of landed gradients (rounds 0 and 1, in two buckets, then one tensor
+    landing again with new values, as a later backward of the same step would) followed by
+    the exchange's own pushes with the landed pieces skipped leave every round's window
+    half exactly as a plain exchange of the final gradients does."""
+    import numpy as np
+    from hybridagent_b200._lib import CHUNK_DTYPE, COPY_DTYPE
+    n = [1000, 64, 5000, 3, 7000, 1, 1234, 6400, 640]
+    p = layout.plan(n, [HA_BF16] * len(n), world)
+    (cls,) = p.classes
+    pc = layout.exchange_pieces(cls, p.owner, n, S)
+    rank, esz, CH = world - 1, 2, 256
+    rng = np.random.default_rng(world * S)
+    present = [k != 2 for k in range(len(cls.indices))]  # entry 2 has no gradient here: zero-filled
+    entry_ptrs = np.array([(10 + k) << 40 if present[k] else 0 for k in range(len(cls.indices))], np.uint64)
+    recv = [(100 + o) << 40 for o in range(world)]
+    dst = layout.piece_destinations(pc, recv, rank, world, esz)
+
+    def memory(grads):
+        mem = {100 + o: np.full(2 * world * S, 0xDEAD, np.uint16) for o in range(world)}
+        mem.update({10 + k: g.copy() for k, g in grads.items()})
+        return mem
+
+    def push_round(mem, k, src):
+        entries = np.nonzero(pc.round == k)[0]
+        copies = np.zeros(len(dst), COPY_DTYPE)
+        copies["src"], copies["dst"], copies["numel"] = src, dst, pc.count
+        per = (pc.count[entries] + CH - 1) // CH
+        chunks = np.zeros(int(per.sum()), CHUNK_DTYPE)
+        chunks["tensor"] = np.repeat(entries, per)
+        chunks["index"] = np.concatenate([np.arange(x) for x in per]) if len(per) else []
+        _emulate_gather(mem, copies, chunks, CH, esz)
+
+    grads = {k: rng.integers(1, 1 << 15, n[i]).astype(np.uint16)
+             for k, i in enumerate(cls.indices) if present[k]}
+    mem = memory(grads)
+    lp = layout.landing_pieces(pc, len(cls.indices))
+    assert sorted(np.concatenate(lp).tolist()) == np.nonzero((pc.round < 2) & (pc.tensor >= 0))[0].tolist()
+    landed_entries = [k for k in grads if len(lp[k])]
+    buckets = [landed_entries[::2], landed_entries[1::2], landed_entries[:1]]
+    for b, bucket in enumerate(buckets):
+        if b == 2:  # a later backward changes the first gradient in place: the second push must win
+            mem[10 + bucket[0]] ^= np.uint16(0x5555)
+        idx = np.concatenate([lp[k] for k in bucket])
+        base = np.concatenate([np.full(len(lp[k]), entry_ptrs[k], np.uint64) for k in bucket])
+        copies, chunks = layout.landing_batch(base + (pc.src_off[idx] * esz).astype(np.uint64), dst[idx],
+                                              pc.count[idx], CH)
+        _emulate_gather(mem, copies, chunks, CH, esz)
+    landed = np.zeros(len(cls.indices), bool)
+    landed[landed_entries] = True
+    src = layout.piece_sources(pc, entry_ptrs, esz, dst, landed)
+    early = (pc.round < 2) & (pc.tensor >= 0) & landed[np.maximum(pc.tensor, 0)]
+    assert early.any() and (src[early] == dst[early]).all() and (src[~early] != dst[~early]).all()
+    # the reference: a plain exchange of the gradients as they are now
+    ref = memory({k: mem[10 + k] for k in grads})
+    src_plain = layout.piece_sources(pc, entry_ptrs, esz)
+    for k in range(pc.n_rounds):
+        push_round(mem, k, src)
+        push_round(ref, k, src_plain)
+        h = (k % 2) * world * S + rank * S
+        for o in range(world):
+            cnt = pc.own_counts(cls, o)[k]
+            assert np.array_equal(mem[100 + o][h:h + cnt], ref[100 + o][h:h + cnt]), (k, o)

@@ -31,12 +31,19 @@ def _gpus() -> int:
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("mode", ["p2p", "p2p_rounds", "nccl"])
+@pytest.mark.parametrize("mode", ["p2p", "p2p_rounds", "nccl", "p2p_landing", "p2p_rounds_landing",
+                                  "p2p_landing_copyengine"])
 @pytest.mark.parametrize("name", ["bf16_world2", "fp32_world2", "bf16_world2_inf"])
 def test_world2_matches_oracle_and_reference(name, mode, tmp_path):
+    """*_landing*: gradients produced by two backward passes and pushed while they land
+    (early pushes in 4 KiB buckets, by the capped kernel or the copy engines), the exchange
+    pushing only the rest."""
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", HYBRIDAGENT_B200_COMM=mode.split("_")[0])
-    if mode == "p2p_rounds":  # a 16 KiB receive window: ~9 exchange rounds of 1024 elements
+    if "rounds" in mode:  # a 16 KiB receive window: ~9 exchange rounds of 1024 elements
         env["HYBRIDAGENT_B200_RECV_BYTES"] = "16384"
+    if "landing" in mode:
+        env.update(WORKER_LANDING="1", HYBRIDAGENT_B200_LAND_BUCKET_BYTES="4096",
+                   HYBRIDAGENT_B200_LAND_CTAS="0" if "copyengine" in mode else "3")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29731",
            os.path.join(HERE, "world_worker.py"), name, str(tmp_path)]
@@ -48,6 +55,8 @@ def test_world2_matches_oracle_and_reference(name, mode, tmp_path):
     assert res[0]["mode"] == res[1]["mode"] == mode.split("_")[0]
     assert res[0]["norms"] == res[1]["norms"]
     assert res[0]["owner"] == g["owner"].tolist()
+    if "landing" in mode:
+        assert all(r["land_launches"] > 0 for r in res)
     for s, (mine, ref) in enumerate(zip(res[0]["norms"], g["norms"].tolist())):
         assert Z.isclose_norm(mine, ref, 1e-6), (s, mine, ref)
     ora, _ = oracle_replay(case, Z.FORM_TORCH_CUDA, norms=res[0]["norms"])

@@ -165,9 +165,14 @@ def main(name: str, out_dir: str) -> None:
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     case = CASES_BY_NAME[name]
+    # gradient landing: the gradients come out of two backward passes that each contribute
+    # half of them (exact in binary floating point), so every landed gradient is pushed
+    # early twice and the second push must win
+    landing = os.environ.get("WORKER_LANDING") == "1"
     params = [torch.nn.Parameter(to_torch(p, case.dtype, s, dev)) for p, s in zip(case.initial_params(), case.shapes)]
     opt = ZeroOneAdamW([{"params": params, "lr": case.lr}], rank=rank, world_size=world, betas=case.betas,
-                       eps=case.eps, weight_decay=case.weight_decay)
+                       eps=case.eps, weight_decay=case.weight_decay, land_grads=landing)
+    assert opt.landing_enabled == (landing and opt.comm_mode == "p2p")
     if case.preload_state:
         for i in opt.param_steps:
             master, m, v, step = case.preload(i)
@@ -182,8 +187,16 @@ def main(name: str, out_dir: str) -> None:
     norms, grads_seen = [], []
     for s in range(case.steps):
         opt.zero_grad(set_to_none=True)
-        for p, g, shape in zip(params, case.grads(s, rank), case.shapes):
-            p.grad = None if g is None else to_torch(g, case.dtype, shape, dev)
+        if landing:
+            half = [None if g is None else to_torch(g, case.dtype, shape, dev) * 0.5
+                    for g, shape in zip(case.grads(s, rank), case.shapes)]
+            for _ in range(2):
+                terms = [(p * h).sum() for p, h in zip(params, half) if h is not None]
+                if terms:
+                    torch.autograd.backward(terms)
+        else:
+            for p, g, shape in zip(params, case.grads(s, rank), case.shapes):
+                p.grad = None if g is None else to_torch(g, case.dtype, shape, dev)
         opt.all_reduce_grads()
         grads_seen.append({i: None if p.grad is None else to_numpy(p.grad, case.dtype) for i, p in enumerate(params)})
         n = opt.clip_grad_norm(case.max_norm)
@@ -192,7 +205,7 @@ def main(name: str, out_dir: str) -> None:
             opt.step()
     torch.cuda.synchronize()
     result = {
-        "rank": rank, "norms": norms, "owner": opt.owner, "mode": opt.comm_mode,
+        "rank": rank, "norms": norms, "owner": opt.owner, "mode": opt.comm_mode, "land_launches": opt.land_launches,
         "params": [to_numpy(p.data, case.dtype) for p in params],
         "state": {i: (to_numpy(opt.master[i], 0), to_numpy(opt.exp_avg[i], 0), to_numpy(opt.exp_avg_sq[i], 0),
                       opt.param_steps[i]) for i in opt.param_steps},
