@@ -245,8 +245,14 @@ def landing_batch(src: np.ndarray, dst: np.ndarray, count: np.ndarray, chunk_ele
 
 def interleaved_chunks(entries: np.ndarray, entry_owner: np.ndarray, entry_numel: np.ndarray, rank: int, world: int,
                        chunk_elems: int) -> np.ndarray:
-    """ha_chunk list over the given table entries, one chunk per owner in turn (starting
-    at owner rank+1, ending with this rank's own), as push_chunk_order explains."""
+    """ha_chunk list over the given table entries (one exchange round's pieces), one chunk
+    per owner in turn, starting at owner rank+1 and ending with this rank's own.
+
+    Chunks run roughly in list order, so a piece-ordered list would keep every in-flight CTA
+    on one destination at a time: local copies and NVLink stores would not overlap, and since
+    every rank walks the pieces in the same order, all ranks would store into the same owner
+    at once and share its ingress.  Taking one chunk per owner in turn, rotated by rank, makes
+    every owner receive from every peer at any moment, with the local copies alongside."""
     per_owner: list[list[tuple[int, int]]] = [[] for _ in range(world)]
     for e in entries.tolist():
         n_chunks = (int(entry_numel[e]) + chunk_elems - 1) // chunk_elems
@@ -265,37 +271,4 @@ def interleaved_chunks(entries: np.ndarray, entry_owner: np.ndarray, entry_numel
     if out:
         tab["tensor"] = [k for k, _ in out]
         tab["index"] = [c for _, c in out]
-    return tab
-
-
-def push_chunk_order(cls: DtypeClass, owner: list[int], rank: int, world: int, numels: list[int],
-                     chunk_elems: int) -> np.ndarray:
-    """ha_chunk list of the gradient push, interleaved across destination owners.
-
-    Chunks run roughly in list order, so a tensor-ordered list keeps every in-flight CTA on
-    one destination at a time: local copies and NVLink stores would not overlap, and since
-    every rank walks the tensors in the same order, all ranks would store into the same
-    owner at once and share its ingress.  Instead each round takes one chunk per owner,
-    starting at owner rank+1 and ending with this rank's own (local) tensors, so at any
-    moment every owner receives from every peer and the local copies run alongside."""
-    per_owner: list[list[tuple[int, int]]] = [[] for _ in range(world)]
-    for k, i in enumerate(cls.indices):
-        n_chunks = (numels[i] + chunk_elems - 1) // chunk_elems
-        per_owner[owner[i]].extend((k, c) for c in range(n_chunks))
-    order = [(rank + d) % world for d in range(1, world + 1)]
-    out = []
-    pos = [0] * world
-    remaining = sum(len(x) for x in per_owner)
-    while remaining:
-        for o in order:
-            if pos[o] < len(per_owner[o]):
-                out.append(per_owner[o][pos[o]])
-                pos[o] += 1
-                remaining -= 1
-    tab = np.zeros(len(out), dtype=_lib.CHUNK_DTYPE)
-    if out:
-        tab["tensor"] = [k for k, _ in out]
-        tab["index"] = [c for _, c in out]
-        sizes = np.ascontiguousarray([numels[i] for i in cls.indices], dtype=np.int64)
-        _lib.call("ha_check_chunks", len(cls.indices), _lib.np_ptr(sizes), _lib.np_ptr(tab), len(tab), chunk_elems)
     return tab

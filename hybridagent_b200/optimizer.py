@@ -240,7 +240,8 @@ class _Class:
             self.land_pieces = layout.landing_pieces(pc, len(cls.indices))
             self.land_mask = (pc.round < layout.LAND_ROUNDS) & (pc.tensor >= 0)
             n_part = max(-(-S // HA_SUM_REGIONS_CHUNK), 1)
-            self.region_partials = [torch.empty(n_part, dtype=torch.float64, device=dev) for _ in range(2)]
+            # one buffer serves every round: the sums run one after another on one stream
+            self.region_partials = torch.empty(n_part, dtype=torch.float64, device=dev)
             self.peers = _lib.Peers()
             deltas = layout.peer_deltas(param_bases, r)
             for q, d in enumerate(deltas):
@@ -435,7 +436,7 @@ class ZeroOneAdamW:
                     count = c.own_counts[k]
                     window = c.recv_buf.ptr + (k % 2) * self.world * S * esz
                     _lib.call("ha_sum_regions", window, self.world, S, count, c.own_grad.data_ptr() + k * S * esz,
-                              c.code, c.region_partials[k % 2].data_ptr(), self._norm_rounds[ci, k:].data_ptr(),
+                              c.code, c.region_partials.data_ptr(), self._norm_rounds[ci, k:].data_ptr(),
                               side.cuda_stream)
                     self.launches += 2 if count else 1
                 self._phase("sum_regions", False)

@@ -38,18 +38,24 @@ def test_mixed_dtype_classes():
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_push_chunk_order_covers_every_chunk_once_and_interleaves_owners(world):
+def test_interleaved_chunks_cover_every_chunk_once_and_interleave_owners(world):
+    """Each exchange round's chunk list (the product's order) covers every chunk of every
+    piece of the round once and visits the owners in turn, starting after this rank."""
+    import numpy as np
     n = workloads.numels(workloads.qwen3_8b())
     p = layout.plan(n, [HA_BF16] * len(n), world)
     (cls,) = p.classes
+    S = layout.round_elems_for(cls, world, 2, 4 << 30)
+    pc = layout.exchange_pieces(cls, p.owner, n, S)
     for rank in range(world):
-        order = layout.push_chunk_order(cls, p.owner, rank, world, n, 16384)
-        natural = layout.chunk_table([n[i] for i in cls.indices], 16384)
-        assert sorted(map(tuple, order.tolist())) == sorted(map(tuple, natural.tolist()))
-        owners = [p.owner[cls.indices[int(t)]] for t in order["tensor"][:4 * world]]
-        # the first rounds visit every owner, starting after this rank and ending with it
-        assert owners[:world] == [(rank + d) % world for d in range(1, world + 1)]
-        assert len(set(owners)) == world
+        for k in range(pc.n_rounds):
+            entries = np.nonzero(pc.round == k)[0]
+            order = layout.interleaved_chunks(entries, pc.owner, pc.count, rank, world, 16384)
+            want = sorted((int(e), c) for e in entries for c in range(-(-int(pc.count[e]) // 16384)))
+            assert sorted(map(tuple, order.tolist())) == want
+            owners = [int(pc.owner[int(t)]) for t in order["tensor"][:world]]
+            # the first pass visits every owner, starting after this rank and ending with it
+            assert owners == [(rank + d) % world for d in range(1, world + 1)]
 
 
 def test_push_destinations_land_in_the_senders_region():
