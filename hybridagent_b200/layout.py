@@ -224,6 +224,18 @@ def piece_sources(pc: Pieces, entry_ptrs: np.ndarray, elem_bytes: int, dst: np.n
     return src
 
 
+def balanced_groups(entries: np.ndarray, sizes: np.ndarray, n: int) -> list[np.ndarray]:
+    """Splits ``entries`` into ``n`` groups of about equal total size (largest first, each to
+    the currently smallest group); each group keeps its entries in their original order."""
+    groups: list[list[int]] = [[] for _ in range(n)]
+    load = [0] * n
+    for j in np.argsort(-np.asarray(sizes, dtype=np.int64), kind="stable").tolist():
+        g = load.index(min(load))
+        groups[g].append(j)
+        load[g] += int(sizes[j])
+    return [np.asarray(entries, dtype=np.int64)[sorted(g)] for g in groups]
+
+
 def landing_batch(src: np.ndarray, dst: np.ndarray, count: np.ndarray, chunk_elems: int) -> tuple[np.ndarray, np.ndarray]:
     """ha_copy entries (piece j: ``count[j]`` elements from address ``src[j]`` to ``dst[j]``)
     and the ha_chunk list that covers them, for one early push of landed gradients."""

@@ -227,9 +227,16 @@ class _Class:
             self.move.np["dst"][:len(dst)] = dst
             self.move.np["numel"][:len(dst)] = pc.count
             self.piece_src_bytes = (pc.src_off * esz).astype(np.uint64)
-            self.round_chunks = []
+            # per round: the push's chunk list (every piece; or, with the copy-engine push, this
+            # rank's own pieces only) and the copy-engine groups of the pieces bound for peers
+            ce = opt.push_streams > 0
+            self.round_chunks, self.round_remote = [], []
             for k in range(pc.n_rounds):
                 entries = np.nonzero(pc.round == k)[0]
+                if ce:
+                    remote = entries[pc.owner[entries] != r]
+                    entries = entries[pc.owner[entries] == r]
+                    self.round_remote.append(layout.balanced_groups(remote, pc.count[remote], opt.push_streams))
                 tab = layout.interleaved_chunks(entries, pc.owner, pc.count, r, W, HA_ADAMW_CHUNK)
                 _lib.call("ha_check_chunks", len(pc.count), _lib.np_ptr(np.ascontiguousarray(pc.count)),
                           _lib.np_ptr(tab), len(tab), HA_ADAMW_CHUNK)
@@ -365,6 +372,12 @@ class ZeroOneAdamW:
         for c in self._classes:
             own = c.packed_param.data_ptr() + self.rank * c.layout.seg_len * c.packed_param.element_size()
             self._comm.all_gather(own, c.packed_param.data_ptr(), c.layout.seg_len, c.code)
+        # HYBRIDAGENT_B200_PUSH_STREAMS=N > 0: the pieces bound for peers go to the copy engines
+        # on N streams, and the SMs only copy this rank's own pieces and sum.  Measured on B200 at
+        # world 2 (Qwen3-8B set): 33.0 ms per step against 36.2 with the kernel push, whose remote
+        # stores need nearly every SM and starve the owner sums; the copy engines move 669 GB/s.
+        # At world > 2 this rank's own share and the sums shrink as 1/W: the kernel push stays.
+        self.push_streams = int(os.environ.get("HYBRIDAGENT_B200_PUSH_STREAMS", "2" if self.world == 2 else "0"))
         want = os.environ.get("HYBRIDAGENT_B200_COMM", "p2p")
         if want not in ("p2p", "nccl"):
             raise ValueError(f"HYBRIDAGENT_B200_COMM={want!r}: expected p2p or nccl")
@@ -392,6 +405,7 @@ class ZeroOneAdamW:
                 c.set_mode(self, None, None)
             c.move.upload()
         self._sum_stream = torch.cuda.Stream(device=self.device) if use_p2p else None
+        self._push_streams = [torch.cuda.Stream(device=self.device) for _ in range(self.push_streams)] if use_p2p else []
         rounds = max(c.pieces.n_rounds for c in self._classes) if use_p2p else 1
         self._norm_rounds = torch.zeros((len(self._classes), rounds), dtype=torch.float64, device=self.device)
         self._norm_rounds_host = torch.zeros((len(self._classes), rounds), dtype=torch.float64, pin_memory=True)
@@ -412,12 +426,24 @@ class ZeroOneAdamW:
         summed = None  # event after the previous round's sums on the side stream
         for k in range(rounds):
             self._phase("push", True)
+            if self._push_streams:  # pieces bound for peers: copy engines, one group per stream
+                ready = torch.cuda.Event()
+                ready.record(main)  # after the tables, the used mask and barrier k-1
+                for j, st in enumerate(self._push_streams):
+                    st.wait_event(ready)
+                    for c in self._classes:
+                        if k < c.pieces.n_rounds and len(c.round_remote[k][j]):
+                            copies = c.move.np[c.round_remote[k][j]]
+                            _lib.call("ha_copy_async", _lib.np_ptr(copies), len(copies),
+                                      c.packed_param.element_size(), st.cuda_stream)
             for c in self._classes:
                 if k < c.pieces.n_rounds and c.round_chunks[k][1]:
                     ch, n = c.round_chunks[k]
                     _lib.call("ha_gather", c.move.ptr, ch.data_ptr(), n, HA_ADAMW_CHUNK,
                               c.packed_param.element_size(), main.cuda_stream)
                     self.launches += 1
+            for st in self._push_streams:
+                main.wait_stream(st)
             self._phase("push", False)
             if summed is not None:
                 main.wait_event(summed)  # this rank has read the half that round k+1 rewrites

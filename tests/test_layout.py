@@ -197,3 +197,15 @@ def test_landing_then_residual_equals_plain_exchange(world, S):
         for o in range(world):
             cnt = pc.own_counts(cls, o)[k]
             assert np.array_equal(mem[100 + o][h:h + cnt], ref[100 + o][h:h + cnt]), (k, o)
+
+
+def test_balanced_groups():
+    import numpy as np
+    entries = np.array([10, 11, 12, 13, 14, 15])
+    sizes = np.array([5, 100, 7, 60, 40, 1])
+    groups = layout.balanced_groups(entries, sizes, 2)
+    assert sorted(np.concatenate(groups).tolist()) == entries.tolist()
+    loads = [int(sizes[np.searchsorted(entries, g)].sum()) for g in groups]
+    assert max(loads) - min(loads) <= max(sizes)
+    assert all((np.diff(g) > 0).all() for g in groups)  # original order kept
+    assert [len(g) for g in layout.balanced_groups(entries[:0], sizes[:0], 3)] == [0, 0, 0]

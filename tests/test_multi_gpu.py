@@ -32,7 +32,7 @@ def _gpus() -> int:
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("mode", ["p2p", "p2p_rounds", "nccl", "p2p_landing", "p2p_rounds_landing",
-                                  "p2p_landing_copyengine"])
+                                  "p2p_landing_copyengine", "p2p_cepush", "p2p_rounds_cepush"])
 @pytest.mark.parametrize("name", ["bf16_world2", "fp32_world2", "bf16_world2_inf"])
 def test_world2_matches_oracle_and_reference(name, mode, tmp_path):
     """*_landing*: gradients produced by two backward passes and pushed while they land
@@ -41,6 +41,9 @@ def test_world2_matches_oracle_and_reference(name, mode, tmp_path):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", HYBRIDAGENT_B200_COMM=mode.split("_")[0])
     if "rounds" in mode:  # a 16 KiB receive window: ~9 exchange rounds of 1024 elements
         env["HYBRIDAGENT_B200_RECV_BYTES"] = "16384"
+    # the peer-bound pieces by the copy engines on 2 streams (the world-2 default: *_cepush and
+    # the landing modes) or by the push kernel (p2p, p2p_rounds)
+    env["HYBRIDAGENT_B200_PUSH_STREAMS"] = "2" if ("cepush" in mode or "landing" in mode) else "0"
     if "landing" in mode:
         env.update(WORKER_LANDING="1", HYBRIDAGENT_B200_LAND_BUCKET_BYTES="4096",
                    HYBRIDAGENT_B200_LAND_CTAS="0" if "copyengine" in mode else "3")
