@@ -39,7 +39,8 @@ def _nccl_include() -> str:
 
 def _sources() -> list[str]:
     files = [os.path.join(CSRC, f) for f in CU_SOURCES + CPP_SOURCES]
-    files += [os.path.join(CSRC, "ha_common.cuh"), os.path.join(INCLUDE, "hybridagent_b200.h"), __file__]
+    files += [os.path.join(CSRC, "ha_common.cuh"), os.path.join(CSRC, "ha_nvtx.h"),
+              os.path.join(INCLUDE, "hybridagent_b200.h"), __file__]
     return files
 
 
@@ -76,8 +77,13 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
         _run([NVCC, "-x", "c++", "-O2", "-std=c++17", "-Wno-deprecated-gpu-targets", "-Xcompiler", "-fPIC,-ffp-contract=off,-Wall", "-I", INCLUDE,
               "-I", _nccl_include(), "-c", os.path.join(CSRC, src), "-o", obj], verbose)
         objs.append(obj)
+    # export the C ABI (ha_*) only: the static CUDA runtime and internal C++ stay local
+    exports = os.path.join(OBJ_DIR, "exports.map")
+    with open(exports, "w") as f:
+        f.write("{ global: ha_*; local: *; };\n")
     tmp = LIB_PATH + ".tmp"
-    _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs, "-ldl", "-lrt", "-lpthread"], verbose)
+    _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs, "-ldl", "-lrt", "-lpthread",
+          "-Xlinker", f"--version-script={exports}"], verbose)
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
 

@@ -189,6 +189,7 @@ __global__ void __launch_bounds__(kThreads) scale_kernel(const ha_tensor* __rest
 extern "C" int ha_adamw_step(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,
                              int64_t chunk_elems, int grad_dtype, int param_dtype, const ha_adamw_scalars* sc,
                              void* stream) {
+  HA_NVTX_RANGE();
   using namespace ha;
   if (chunk_elems != HA_ADAMW_CHUNK) return fail(HA_ERR_INVALID, "ha_adamw_step: chunk_elems must be %d", HA_ADAMW_CHUNK);
   if (!valid_float_dtype(grad_dtype)) return fail(HA_ERR_UNSUPPORTED, "ha_adamw_step: grad dtype %d", grad_dtype);
@@ -213,6 +214,7 @@ extern "C" int ha_adamw_step(const ha_tensor* d_tensors, const ha_chunk* d_chunk
 extern "C" int ha_adamw_step_peers(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,
                                    int64_t chunk_elems, int grad_dtype, int param_dtype, const ha_adamw_scalars* sc,
                                    const ha_peers* peers, void* stream) {
+  HA_NVTX_RANGE();
   using namespace ha;
   if (chunk_elems != HA_ADAMW_CHUNK)
     return fail(HA_ERR_INVALID, "ha_adamw_step_peers: chunk_elems must be %d", HA_ADAMW_CHUNK);
@@ -243,6 +245,7 @@ extern "C" int ha_adamw_step_peers(const ha_tensor* d_tensors, const ha_chunk* d
 
 extern "C" int ha_scale_grads(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,
                               int64_t chunk_elems, int grad_dtype, float mult, void* stream) {
+  HA_NVTX_RANGE();
   using namespace ha;
   if (chunk_elems != HA_ADAMW_CHUNK) return fail(HA_ERR_INVALID, "ha_scale_grads: chunk_elems must be %d", HA_ADAMW_CHUNK);
   if (!valid_float_dtype(grad_dtype)) return fail(HA_ERR_UNSUPPORTED, "ha_scale_grads: grad dtype %d", grad_dtype);

@@ -16,6 +16,7 @@
 #include <nccl.h>
 
 #include "hybridagent_b200.h"
+#include "ha_nvtx.h"
 
 namespace ha {
 int fail(int code, const char* fmt, ...);
@@ -140,6 +141,7 @@ int usable(ha_comm* comm, const char* what) {
 }  // namespace
 
 extern "C" int ha_reduce_scatter(ha_comm* comm, const void* send, void* recv, size_t count, int dtype, void* stream) {
+  HA_NVTX_RANGE();
   ncclDataType_t t;
   if (int rc = usable(comm, "ha_reduce_scatter")) return rc;
   if (!nccl_type(dtype, &t)) return ha::fail(HA_ERR_INVALID, "ha_reduce_scatter: bad arguments");
@@ -148,6 +150,7 @@ extern "C" int ha_reduce_scatter(ha_comm* comm, const void* send, void* recv, si
 }
 
 extern "C" int ha_all_gather(ha_comm* comm, const void* send, void* recv, size_t count, int dtype, void* stream) {
+  HA_NVTX_RANGE();
   ncclDataType_t t;
   if (int rc = usable(comm, "ha_all_gather")) return rc;
   if (!nccl_type(dtype, &t)) return ha::fail(HA_ERR_INVALID, "ha_all_gather: bad arguments");
@@ -156,6 +159,7 @@ extern "C" int ha_all_gather(ha_comm* comm, const void* send, void* recv, size_t
 }
 
 extern "C" int ha_all_reduce_sum(ha_comm* comm, void* buf, size_t count, int dtype, void* stream) {
+  HA_NVTX_RANGE();
   ncclDataType_t t;
   if (int rc = usable(comm, "ha_all_reduce_sum")) return rc;
   if (!nccl_type(dtype, &t)) return ha::fail(HA_ERR_INVALID, "ha_all_reduce_sum: bad arguments");
@@ -164,6 +168,7 @@ extern "C" int ha_all_reduce_sum(ha_comm* comm, void* buf, size_t count, int dty
 }
 
 extern "C" int ha_all_reduce_max(ha_comm* comm, void* buf, size_t count, int dtype, void* stream) {
+  HA_NVTX_RANGE();
   ncclDataType_t t;
   if (int rc = usable(comm, "ha_all_reduce_max")) return rc;
   if (!nccl_type(dtype, &t)) return ha::fail(HA_ERR_INVALID, "ha_all_reduce_max: bad arguments");

@@ -124,17 +124,20 @@ int launch_gather(const ha_copy* d_copies, const ha_chunk* d_chunks, int64_t n_c
 
 extern "C" int ha_gather(const ha_copy* d_copies, const ha_chunk* d_chunks, int64_t n_chunks, int64_t chunk_elems,
                          int elem_bytes, void* stream) {
+  HA_NVTX_RANGE();
   return ha::launch_gather(d_copies, d_chunks, n_chunks, chunk_elems, elem_bytes, 0, stream, "ha_gather");
 }
 
 extern "C" int ha_gather_capped(const ha_copy* d_copies, const ha_chunk* d_chunks, int64_t n_chunks,
                                 int64_t chunk_elems, int elem_bytes, int32_t max_ctas, void* stream) {
+  HA_NVTX_RANGE();
   if (max_ctas <= 0) return ha::fail(HA_ERR_INVALID, "ha_gather_capped: max_ctas %d", max_ctas);
   return ha::launch_gather(d_copies, d_chunks, n_chunks, chunk_elems, elem_bytes, max_ctas, stream,
                            "ha_gather_capped");
 }
 
 extern "C" int ha_copy_async(const ha_copy* h_copies, int64_t n, int elem_bytes, void* stream) {
+  HA_NVTX_RANGE();
   if (elem_bytes != 2 && elem_bytes != 4) return ha::fail(HA_ERR_UNSUPPORTED, "ha_copy_async: elem_bytes %d", elem_bytes);
   if (n < 0 || (n > 0 && h_copies == nullptr)) return ha::fail(HA_ERR_INVALID, "ha_copy_async: %lld entries", (long long)n);
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -138,6 +138,7 @@ __global__ void __launch_bounds__(kFinalThreads) finalize_kernel(const double* _
 
 extern "C" int ha_grad_sumsq(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,
                              int64_t chunk_elems, int grad_dtype, double* d_partials, double* d_out, void* stream) {
+  HA_NVTX_RANGE();
   using namespace ha;
   if (chunk_elems != HA_SUMSQ_CHUNK) return fail(HA_ERR_INVALID, "ha_grad_sumsq: chunk_elems must be %d", HA_SUMSQ_CHUNK);
   if (!valid_float_dtype(grad_dtype)) return fail(HA_ERR_UNSUPPORTED, "ha_grad_sumsq: grad dtype %d", grad_dtype);
@@ -205,6 +206,7 @@ int noalloc_partials(double** out) {
 
 extern "C" int ha_grad_sumsq_noalloc(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,
                                      int64_t chunk_elems, int grad_dtype, double* d_out, void* stream) {
+  HA_NVTX_RANGE();
   using namespace ha;
   if (chunk_elems != HA_SUMSQ_CHUNK)
     return fail(HA_ERR_INVALID, "ha_grad_sumsq_noalloc: chunk_elems must be %d", HA_SUMSQ_CHUNK);

@@ -13,6 +13,7 @@
 #include <stdint.h>
 
 #include "hybridagent_b200.h"
+#include "ha_nvtx.h"
 
 namespace ha {
 

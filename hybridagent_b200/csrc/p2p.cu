@@ -156,6 +156,7 @@ extern "C" int ha_free(void* ptr) {
 }
 
 extern "C" int ha_memset(void* ptr, int value, size_t bytes, void* stream) {
+  HA_NVTX_RANGE();
   if (ptr == nullptr && bytes > 0) return ha::fail(HA_ERR_INVALID, "ha_memset: NULL");
   return ha::cuda_status(cudaMemsetAsync(ptr, value, bytes, static_cast<cudaStream_t>(stream)), "cudaMemsetAsync");
 }
@@ -184,6 +185,7 @@ extern "C" int ha_ipc_close(void* ptr) {
 
 extern "C" int ha_sum_regions(const void* d_regions, int32_t world, int64_t region_elems, int64_t count,
                               void* d_sum, int dtype, double* d_partials, double* d_out, void* stream) {
+  HA_NVTX_RANGE();
   using namespace ha;
   if (!valid_float_dtype(dtype)) return fail(HA_ERR_UNSUPPORTED, "ha_sum_regions: dtype %d", dtype);
   if (world < 1 || world > kMaxWorld)

@@ -60,6 +60,7 @@ Deliberate differences (documented surface):
 from __future__ import annotations
 
 import ctypes
+import functools
 import os
 import weakref
 from collections.abc import MutableMapping
@@ -72,6 +73,20 @@ from ._lib import (HA_ADAMW_CHUNK, HA_BF16, HA_F16, HA_F32, HA_F64, HA_I32, HA_S
                    HA_U8)
 
 _CODES = {torch.float32: HA_F32, torch.bfloat16: HA_BF16, torch.float16: HA_F16}
+
+
+def _nvtx(fn):
+    """An NVTX range named ZeroOneAdamW.<method> around each call."""
+    name = f"ZeroOneAdamW.{fn.__name__}"
+
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        torch.cuda.nvtx.range_push(name)
+        try:
+            return fn(*args, **kwargs)
+        finally:
+            torch.cuda.nvtx.range_pop()
+    return wrapper
 _TORCH = {v: k for k, v in _CODES.items()}
 STATE_FORMAT = "hybridagent_b200.zero1_adamw/1"
 
@@ -477,6 +492,12 @@ class ZeroOneAdamW:
 
     # ---------------------------------------------------------------- helpers
     def _phase(self, name: str, start: bool) -> None:
+        """Marks a phase: an NVTX range (Nsight timelines) and, if a timer is attached, its
+        CUDA events."""
+        if start:
+            torch.cuda.nvtx.range_push(f"ZeroOneAdamW.{name}")
+        else:
+            torch.cuda.nvtx.range_pop()
         if self.timer is not None:
             (self.timer.begin if start else self.timer.end)(name)
 
@@ -674,6 +695,7 @@ class ZeroOneAdamW:
             elif parameter.grad is not None:
                 parameter.grad.zero_()
 
+    @_nvtx
     @torch.no_grad()
     def all_reduce_grads(self) -> None:
         """Sum every rank's gradient onto its owner (optimizer.py:95-143).  Tensors with no
@@ -763,6 +785,7 @@ class ZeroOneAdamW:
             # them unless an owned gradient is replaced before it runs
             self._fused_sumsq = [self.params[i].grad for c in self._classes for i in c.owned] if p2p else None
 
+    @_nvtx
     @torch.no_grad()
     def clip_grad_norm(self, max_norm: float) -> float:
         """Global L2 norm of the owned gradients (all ranks), clipping to max_norm
@@ -806,6 +829,7 @@ class ZeroOneAdamW:
             self._pending_clip = float(max_norm) / (norm + 1e-6)  # optimizer.py:156
         return norm
 
+    @_nvtx
     @torch.no_grad()
     def apply_pending_clip(self) -> None:
         """Scales the owned gradients in place by the factor the last clip_grad_norm chose
@@ -833,6 +857,7 @@ class ZeroOneAdamW:
                     if g is not None and g is not self.params[i].grad:
                         self.params[i].grad.copy_(g)
 
+    @_nvtx
     @torch.no_grad()
     def step(self) -> None:
         """Fused AdamW over the owned tensors with a gradient, then the parameter

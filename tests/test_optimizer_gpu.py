@@ -220,3 +220,36 @@ def test_checkpoint_files_resume_bit_identically(tmp_path):
         assert torch.equal(params[i].data, fresh[i].data)
         assert torch.equal(opt.exp_avg_sq[i], opt2.exp_avg_sq[i]) and torch.equal(opt.master[i], opt2.master[i])
         assert opt.param_steps[i] == opt2.param_steps[i]
+
+
+def test_ten_thousand_ragged_tensors():
+    """10,000 tensors of every small length (every numel mod 8, 1-element tensors, a few
+    multi-chunk ones) through the public API, two clipped steps with some gradients absent:
+    every element bit for bit equal to the oracle (the MoE set's 11,852-tensor scale)."""
+    from cases import BF16, Case
+    rng = np.random.default_rng(10_000)
+    sizes = [int(n) for n in rng.integers(1, 300, 10_000)]
+    sizes[:8] = [1, 2, 3, 4, 5, 6, 7, 8]
+    sizes[100:103] = [16383, 16385, 70001]
+    overrides = {(s, -1, int(i)): "none" for s in range(2) for i in rng.integers(0, len(sizes), 50)}
+    case = Case("many_tensors", 99, [(n,) for n in sizes], BF16, steps=2, grad_sigma=3e-2, lr=1e-3,
+                overrides=overrides)
+    params, opt = build(case)
+    norms = run_steps(case, params, opt, range(case.steps))
+    assert all(math.isfinite(n) and n > case.max_norm for n in norms)  # clip active
+    ora, _ = oracle_replay(case, Z.FORM_TORCH_CUDA, norms=norms)
+    got_master = to_numpy(torch_cat([opt.master[i].reshape(-1) for i in range(len(sizes))]), 0)
+    got_m = to_numpy(torch_cat([opt.exp_avg[i].reshape(-1) for i in range(len(sizes))]), 0)
+    got_v = to_numpy(torch_cat([opt.exp_avg_sq[i].reshape(-1) for i in range(len(sizes))]), 0)
+    got_p = to_numpy(torch_cat([p.data.reshape(-1) for p in params]), case.dtype)
+    want = [ora.tensor_state(i) for i in range(len(sizes))]
+    assert_bits_equal(got_master, np.concatenate([w[0] for w in want]), "master")
+    assert_bits_equal(got_m, np.concatenate([w[1] for w in want]), "exp_avg")
+    assert_bits_equal(got_v, np.concatenate([w[2] for w in want]), "exp_avg_sq")
+    assert_bits_equal(got_p, np.concatenate(ora.params), "param")
+    assert [opt.param_steps[i] for i in range(len(sizes))] == [w[3] for w in want]
+
+
+def torch_cat(ts):
+    import torch
+    return torch.cat(ts)
