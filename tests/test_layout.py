@@ -209,3 +209,24 @@ def test_balanced_groups():
     assert max(loads) - min(loads) <= max(sizes)
     assert all((np.diff(g) > 0).all() for g in groups)  # original order kept
     assert [len(g) for g in layout.balanced_groups(entries[:0], sizes[:0], 3)] == [0, 0, 0]
+
+
+@pytest.mark.parametrize("S", [64, 64 * 4, 64 * 1000])
+def test_empty_owner_segments(S):
+    """More ranks than tensors: the ranks that own nothing have an empty padded load, receive
+    no pieces, reduce nothing in any round and land nothing early."""
+    import numpy as np
+    n = [1000, 64, 5]
+    p = layout.plan(n, [HA_BF16] * len(n), 5)
+    (cls,) = p.classes
+    assert sorted(p.owner) == [0, 1, 2]
+    assert [cls.own_len[r] for r in (3, 4)] == [0, 0]
+    pc = layout.exchange_pieces(cls, p.owner, n, S)
+    assert not np.isin(pc.owner, [3, 4]).any()
+    for r in (3, 4):
+        assert pc.own_counts(cls, r) == [0] * pc.n_rounds
+        assert cls.owned(p.owner, r) == []
+    lp = layout.landing_pieces(pc, len(cls.indices))
+    assert sum(len(x) for x in lp) == int(((pc.round < 2) & (pc.tensor >= 0)).sum())
+    dst = layout.piece_destinations(pc, [(10 + r) << 40 for r in range(5)], 4, 5, 2)
+    assert ((dst >> np.uint64(40)) - np.uint64(10) < np.uint64(3)).all()  # only owners 0-2 receive

@@ -105,7 +105,8 @@ def test_stalled_peer_raises_comm_failure(tmp_path):
 @pytest.mark.parametrize("mode", ["p2p", "p2p_rounds", "nccl"])
 def test_world2_mixed_dtype_classes(mode, tmp_path):
     """bf16 + fp32 + fp16 parameters in one optimizer (three dtype classes, each exchanged
-    in its own rounds), a tensor absent on one rank: bit for bit against the oracle."""
+    in its own rounds; the single fp16 tensor leaves one rank an empty fp16 segment), a tensor
+    absent on one rank: bit for bit against the oracle."""
     sys.path.insert(0, HERE)
     from world_worker import mixed_grads, mixed_spec
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", HYBRIDAGENT_B200_COMM=mode.split("_")[0])

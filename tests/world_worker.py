@@ -135,8 +135,9 @@ def mixed(out_dir: str) -> None:
 
 def mixed_spec():
     from helpers import Z
+    # one fp16 tensor: the other rank's fp16 segment is empty
     return [((64, 96), Z.BF16), ((33,), Z.F32), ((1000,), Z.BF16), ((48, 16), Z.F32), ((40, 24), Z.F16),
-            ((4097,), Z.BF16), ((7,), Z.F16), ((256, 64), Z.F32)]
+            ((4097,), Z.BF16), ((7,), Z.BF16), ((256, 64), Z.F32)]
 
 
 def mixed_grads(step, rank):
