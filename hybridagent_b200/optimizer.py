@@ -957,22 +957,32 @@ class ZeroOneAdamW:
 
     def close(self) -> None:
         """Releases the peer mappings and the NCCL communicator (world_size > 1).  Call it on
-        every rank after the last step."""
+        every rank after the last step: it waits for all of this rank's work (pushes, sums,
+        early pushes included) and, at world > 1, for every rank to reach it (a barrier under
+        the communicator's deadline), so no rank releases memory a peer still writes."""
+        self._release(collective=True)
+
+    def _release(self, collective: bool) -> None:
         for h in getattr(self, "_land_hooks", []):
             h.remove()
         self._land_hooks = []
         self.landing_enabled = False
-        if self._peer_map is not None:
-            torch.cuda.current_stream(self.device).synchronize()
+        if getattr(self, "_peer_map", None) is not None:
+            torch.cuda.synchronize(self.device)  # every stream of this rank, peer stores included
+            if collective and self._comm is not None and self._comm.failure is None:
+                with torch.cuda.device(self.device):
+                    self._barrier()
+                    self._comm.read(self._barrier_buf, torch.zeros(1, dtype=torch.int32, pin_memory=True),
+                                    "barrier before releasing the peer mappings")
             self._peer_map.close()
             self._peer_map = None
-        if self._comm is not None:
+        if getattr(self, "_comm", None) is not None:
             self._comm.close()
             self._comm = None
 
     def __del__(self):
         try:
-            self.close()
+            self._release(collective=False)  # never a collective from the garbage collector
         except Exception:
             pass
 
