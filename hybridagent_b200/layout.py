@@ -224,6 +224,20 @@ def piece_sources(pc: Pieces, entry_ptrs: np.ndarray, elem_bytes: int, dst: np.n
     return src
 
 
+def split_smallest(entries: np.ndarray, sizes: np.ndarray, share: float) -> tuple[np.ndarray, np.ndarray]:
+    """(rest, smallest): the smallest entries whose sizes add up to at most ``share`` of the
+    total go to the second array; both keep the original order."""
+    entries = np.asarray(entries, dtype=np.int64)
+    if share <= 0 or len(entries) == 0:
+        return entries, entries[:0]
+    sizes = np.asarray(sizes, dtype=np.int64)
+    order = np.argsort(sizes, kind="stable")
+    take = order[np.cumsum(sizes[order]) <= share * int(sizes.sum())]
+    mask = np.zeros(len(entries), dtype=bool)
+    mask[take] = True
+    return entries[~mask], entries[mask]
+
+
 def balanced_groups(entries: np.ndarray, sizes: np.ndarray, n: int) -> list[np.ndarray]:
     """Splits ``entries`` into ``n`` groups of about equal total size (largest first, each to
     the currently smallest group); each group keeps its entries in their original order."""

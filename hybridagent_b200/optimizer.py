@@ -250,7 +250,8 @@ class _Class:
                 entries = np.nonzero(pc.round == k)[0]
                 if ce:
                     remote = entries[pc.owner[entries] != r]
-                    entries = entries[pc.owner[entries] == r]
+                    remote, by_kernel = layout.split_smallest(remote, pc.count[remote], opt.push_kernel_share)
+                    entries = np.sort(np.concatenate([entries[pc.owner[entries] == r], by_kernel]))
                     self.round_remote.append(layout.balanced_groups(remote, pc.count[remote], opt.push_streams))
                 tab = layout.interleaved_chunks(entries, pc.owner, pc.count, r, W, HA_ADAMW_CHUNK)
                 _lib.call("ha_check_chunks", len(pc.count), _lib.np_ptr(np.ascontiguousarray(pc.count)),
@@ -393,6 +394,10 @@ class ZeroOneAdamW:
         # stores need nearly every SM and starve the owner sums; the copy engines move 669 GB/s.
         # At world > 2 this rank's own share and the sums shrink as 1/W: the kernel push stays.
         self.push_streams = int(os.environ.get("HYBRIDAGENT_B200_PUSH_STREAMS", "2" if self.world == 2 else "0"))
+        # with the copy-engine push: the share of the peer-bound bytes (smallest pieces first) that
+        # the push kernel stores instead, using SM time the local copies and sums leave idle and
+        # link bandwidth the copy engines leave unused (world 2: 0.1 -> 32.4 ms, 0 -> 33.0, 0.2 -> 32.7)
+        self.push_kernel_share = float(os.environ.get("HYBRIDAGENT_B200_PUSH_KERNEL_SHARE", "0.1"))
         want = os.environ.get("HYBRIDAGENT_B200_COMM", "p2p")
         if want not in ("p2p", "nccl"):
             raise ValueError(f"HYBRIDAGENT_B200_COMM={want!r}: expected p2p or nccl")

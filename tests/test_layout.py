@@ -230,3 +230,15 @@ def test_empty_owner_segments(S):
     assert sum(len(x) for x in lp) == int(((pc.round < 2) & (pc.tensor >= 0)).sum())
     dst = layout.piece_destinations(pc, [(10 + r) << 40 for r in range(5)], 4, 5, 2)
     assert ((dst >> np.uint64(40)) - np.uint64(10) < np.uint64(3)).all()  # only owners 0-2 receive
+
+
+def test_split_smallest():
+    import numpy as np
+    e = np.array([5, 6, 7, 8, 9])
+    sz = np.array([50, 10, 30, 5, 100])
+    rest, small = layout.split_smallest(e, sz, 0.2)  # 20% of 195 = 39: sizes 5, 10 (15), +30 > 39
+    assert small.tolist() == [6, 8] and rest.tolist() == [5, 7, 9]
+    rest, small = layout.split_smallest(e, sz, 0.0)
+    assert small.tolist() == [] and rest.tolist() == e.tolist()
+    rest, small = layout.split_smallest(e, sz, 1.0)
+    assert small.tolist() == e.tolist() and rest.tolist() == []
