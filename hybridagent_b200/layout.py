@@ -250,6 +250,21 @@ def balanced_groups(entries: np.ndarray, sizes: np.ndarray, n: int) -> list[np.n
     return [np.asarray(entries, dtype=np.int64)[sorted(g)] for g in groups]
 
 
+def round_push_split(pc: Pieces, k: int, rank: int, push_streams: int,
+                     kernel_share: float) -> tuple[np.ndarray, list[np.ndarray]]:
+    """Round k's pieces split between the push kernel and the copy engines.  With
+    ``push_streams`` 0 the kernel pushes every piece; otherwise it takes this rank's own
+    pieces and the smallest peer-bound ones (``kernel_share`` of their bytes), and the rest
+    go to ``push_streams`` copy-engine groups of about equal bytes."""
+    entries = np.nonzero(pc.round == k)[0]
+    if push_streams <= 0:
+        return entries, []
+    remote = entries[pc.owner[entries] != rank]
+    remote, by_kernel = split_smallest(remote, pc.count[remote], kernel_share)
+    kernel = np.sort(np.concatenate([entries[pc.owner[entries] == rank], by_kernel]))
+    return kernel, balanced_groups(remote, pc.count[remote], push_streams)
+
+
 def landing_batch(src: np.ndarray, dst: np.ndarray, count: np.ndarray, chunk_elems: int) -> tuple[np.ndarray, np.ndarray]:
     """ha_copy entries (piece j: ``count[j]`` elements from address ``src[j]`` to ``dst[j]``)
     and the ha_chunk list that covers them, for one early push of landed gradients."""

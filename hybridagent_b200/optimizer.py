@@ -244,15 +244,10 @@ class _Class:
             self.piece_src_bytes = (pc.src_off * esz).astype(np.uint64)
             # per round: the push's chunk list (every piece; or, with the copy-engine push, this
             # rank's own pieces only) and the copy-engine groups of the pieces bound for peers
-            ce = opt.push_streams > 0
             self.round_chunks, self.round_remote = [], []
             for k in range(pc.n_rounds):
-                entries = np.nonzero(pc.round == k)[0]
-                if ce:
-                    remote = entries[pc.owner[entries] != r]
-                    remote, by_kernel = layout.split_smallest(remote, pc.count[remote], opt.push_kernel_share)
-                    entries = np.sort(np.concatenate([entries[pc.owner[entries] == r], by_kernel]))
-                    self.round_remote.append(layout.balanced_groups(remote, pc.count[remote], opt.push_streams))
+                entries, groups = layout.round_push_split(pc, k, r, opt.push_streams, opt.push_kernel_share)
+                self.round_remote.append(groups)
                 tab = layout.interleaved_chunks(entries, pc.owner, pc.count, r, W, HA_ADAMW_CHUNK)
                 _lib.call("ha_check_chunks", len(pc.count), _lib.np_ptr(np.ascontiguousarray(pc.count)),
                           _lib.np_ptr(tab), len(tab), HA_ADAMW_CHUNK)

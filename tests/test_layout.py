@@ -242,3 +242,33 @@ def test_split_smallest():
     assert small.tolist() == [] and rest.tolist() == e.tolist()
     rest, small = layout.split_smallest(e, sz, 1.0)
     assert small.tolist() == e.tolist() and rest.tolist() == []
+
+
+@pytest.mark.parametrize("world,streams,share", [(2, 0, 0.1), (2, 2, 0.0), (2, 2, 0.1), (3, 4, 0.3), (8, 2, 0.1)])
+def test_round_push_split_partitions_every_round(world, streams, share):
+    """Kernel list and copy-engine groups partition each round's pieces; the copy engines get
+    only peer-bound pieces, the kernel every piece of this rank's own and at most the share of
+    the peer-bound bytes (smallest first)."""
+    import numpy as np
+    n = workloads.numels(workloads.qwen3_8b())[:60]
+    p = layout.plan(n, [HA_BF16] * len(n), world)
+    (cls,) = p.classes
+    pc = layout.exchange_pieces(cls, p.owner, n, 64 * 100_000)
+    for rank in range(world):
+        for k in range(pc.n_rounds):
+            kernel, groups = layout.round_push_split(pc, k, rank, streams, share)
+            ce = np.concatenate(groups) if groups else np.zeros(0, np.int64)
+            everything = np.nonzero(pc.round == k)[0]
+            assert sorted(kernel.tolist() + ce.tolist()) == everything.tolist()
+            assert (np.diff(kernel) > 0).all()
+            if streams == 0:
+                assert groups == [] and kernel.tolist() == everything.tolist()
+                continue
+            assert len(groups) == streams and (pc.owner[ce] != rank).all()
+            own = everything[pc.owner[everything] == rank]
+            assert np.isin(own, kernel).all()
+            by_kernel = kernel[pc.owner[kernel] != rank]
+            remote_bytes = int(pc.count[everything[pc.owner[everything] != rank]].sum())
+            assert int(pc.count[by_kernel].sum()) <= share * remote_bytes
+            if len(by_kernel) and len(ce):
+                assert pc.count[by_kernel].max() <= pc.count[ce].min()  # the smallest ones
