@@ -227,9 +227,14 @@ class OracleZeroOne:
         self.step_count = 0
         self.grads: list[np.ndarray | None] = [None] * len(self.params)  # owner-side reduced grads
 
-    def reduce_grads(self, per_rank: list[list[np.ndarray | None]]) -> None:
+    def reduce_grads(self, per_rank: list[list[np.ndarray | None]], round_once: bool = False) -> None:
         """all_reduce_grads (optimizer.py:95-143): used = any rank has a grad; the owner
-        receives the sum, missing grads counting as zeros.  W == 1 keeps the grads."""
+        receives the sum, missing grads counting as zeros.  W == 1 keeps the grads.
+
+        16-bit sums round after every addition in rank order (a chain of reductions in the
+        gradient dtype, as a per-hop reduce does); ``round_once`` instead adds in fp32 in rank
+        order and rounds once (the peer-to-peer owner sum of the B200 build).  The two agree at
+        W = 2, where either rounds the one fp32 sum once."""
         if self.world == 1:
             self.grads = [None if g is None else g.reshape(-1).copy() for g in per_rank[0]]
             return
@@ -242,7 +247,12 @@ class OracleZeroOne:
             dt = self.dtypes[i]
             filled = [np.zeros(self.params[i].size, np.float32 if dt == F32 else np.uint16) if g is None
                       else g.reshape(-1) for g in present]
-            if dt == BF16:
+            if round_once and dt != F32:
+                acc = widen(filled[0], dt).astype(np.float32).copy()
+                for g in filled[1:]:
+                    acc = acc + widen(g, dt).astype(np.float32)
+                out.append(narrow(acc, dt))
+            elif dt == BF16:
                 out.append(bf16_rank_sum(filled))
             elif dt == F32:
                 acc = filled[0].astype(np.float32).copy()

@@ -195,7 +195,7 @@ def _rank_main_p2p(rank, world, port, name, queue):
         npdt = np.uint16 if case.dtype == Z.BF16 else np.float32
         esz = np.dtype(npdt).itemsize
         SPACE = 1 << 40
-        S = 64 * 20  # small rounds: slots straddle rounds and both halves of the window are used
+        S = 64 * max(2, 40 // world)  # small rounds: slots straddle rounds, both window halves are used
         recv_bases = [(r + 1) * SPACE for r in range(world)]               # each rank's receive window
         param_bases = [(r + 1) * SPACE + SPACE // 2 for r in range(world)]  # each rank's packed params
         pieces = layout.exchange_pieces(cls, plan.owner, numels, S)
@@ -316,3 +316,50 @@ def test_world2_p2p_host_path_matches_reference(name):
         assert_state_close(v, g[f"exp_avg_sq_{i}"], f"exp_avg_sq[{i}]", max_ulp=3)
         assert_state_close(master, g[f"master_{i}"], f"master[{i}]")
         assert_bits_equal(Z.narrow(master, Z.BF16), a, f"param[{i}]")
+
+
+@pytest.mark.parametrize("world", [3, 4])
+def test_p2p_host_path_beyond_two_ranks_matches_oracle(world):
+    """The p2p data flow at W = 3 and 4 (gloo ranks on CPU; the GPU tests run W = 2 only):
+    the product's piece layout, window addresses, rounds and peer offsets with the owner
+    summing every rank's region in fp32 and rounding once, against the oracle's W-rank run
+    with that reduction -- norms within 1e-6, states and parameters bit for bit."""
+    import torch.multiprocessing as mp
+
+    from helpers import Z, assert_bits_equal
+
+    name = "bf16_world2"  # its shapes, value distributions and absent gradients, over W ranks
+    case = CASES_BY_NAME[name]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main_p2p, args=(r, world, port, name, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in procs:
+        rank, norms, final, state, owner = q.get(timeout=300)
+        results[rank] = (norms, final, state, owner)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    norms = results[0][0]
+    assert all(results[r][0] == norms for r in range(world))
+    ora = Z.OracleZeroOne(case.initial_params(), [case.dtype] * len(case.shapes), [case.lr] * len(case.shapes),
+                          world=world, betas=case.betas, eps=case.eps, weight_decay=case.weight_decay)
+    assert ora.owner == results[0][3]
+    for s in range(case.steps):
+        ora.reduce_grads([case.grads(s, r) for r in range(world)], round_once=True)
+        assert Z.isclose_norm(norms[s], Z.norm_from_sumsq(ora.sumsq()), 1e-6), s
+        ora.clip_grad_norm(case.max_norm, norm=norms[s])
+        ora.step()
+    for i in range(len(case.shapes)):
+        for r in range(1, world):
+            assert np.array_equal(results[0][1][i].view(np.uint8), results[r][1][i].view(np.uint8)), (i, r)
+        assert_bits_equal(results[0][1][i], ora.params[i], f"param[{i}]")
+        master, m, v, steps = results[ora.owner[i]][2][i]
+        om, oea, oeas, osteps = ora.tensor_state(i)
+        assert steps == osteps
+        assert_bits_equal(master, om, f"master[{i}]")
+        assert_bits_equal(m, oea, f"exp_avg[{i}]")
+        assert_bits_equal(v, oeas, f"exp_avg_sq[{i}]")
