@@ -603,6 +603,9 @@ class ZeroOneAdamW:
     def _on_landed(self, i: int, p: torch.Tensor) -> None:
         """Post-accumulate-grad hook of parameter i (runs on the autograd engine's thread)."""
         if not (self.landing_enabled and self._land_ok):
+            # the gradient changed (in place, keeping its identity) after any earlier early push:
+            # forget that push so the exchange sends the gradient whole
+            self._landed.pop(i, None)
             return
         ci, k = self._entry_of[i]
         c = self._classes[ci]

@@ -272,3 +272,4 @@ def test_round_push_split_partitions_every_round(world, streams, share):
             assert int(pc.count[by_kernel].sum()) <= share * remote_bytes
             if len(by_kernel) and len(ce):
                 assert pc.count[by_kernel].max() <= pc.count[ce].min()  # the smallest ones
+
