@@ -1,0 +1,88 @@
+"""Property tests (hypothesis) of the shard layout and the exchange plan over random tensor
+lists, world sizes and round sizes: the host logic that decides every address the kernels
+write.  CPU only."""
+import numpy as np
+from hypothesis import given, settings
+from hypothesis import strategies as st
+
+from hybridagent_b200 import layout
+from hybridagent_b200._lib import HA_BF16
+from oracle import zero1 as Z
+
+sizes_st = st.lists(st.integers(min_value=1, max_value=5000), min_size=1, max_size=40)
+world_st = st.integers(min_value=1, max_value=9)
+rounds_st = st.integers(min_value=1, max_value=80)  # round size in units of ALIGN elements
+
+
+@settings(max_examples=150, deadline=None)
+@given(sizes_st, world_st)
+def test_plan_slots_are_aligned_disjoint_and_owned_by_the_greedy_rule(numels, world):
+    p = layout.plan(numels, [HA_BF16] * len(numels), world)
+    assert p.owner == Z.greedy_owners(numels, world)
+    (cls,) = p.classes
+    for r in range(world):
+        mine = sorted((cls.offset[i], numels[i]) for i in cls.indices if p.owner[i] == r)
+        end = 0
+        for off, n in mine:
+            assert off % layout.ALIGN == 0 and off >= end
+            end = off + n
+        assert cls.own_len[r] == layout.align_up(end) if mine else cls.own_len[r] == 0
+        assert cls.own_len[r] <= cls.seg_len
+
+
+@settings(max_examples=150, deadline=None)
+@given(sizes_st, st.integers(min_value=2, max_value=9), rounds_st)
+def test_exchange_pieces_write_every_summed_element_once_per_round(numels, world, units):
+    p = layout.plan(numels, [HA_BF16] * len(numels), world)
+    (cls,) = p.classes
+    S = units * layout.ALIGN
+    pc = layout.exchange_pieces(cls, p.owner, numels, S)
+    written = {}
+    covered = {i: np.zeros(numels[i], np.int8) for i in cls.indices}
+    for t, so, o, do, c, r in zip(pc.tensor, pc.src_off, pc.owner, pc.dst_off, pc.count, pc.round):
+        assert c > 0 and 0 <= do and do + c <= S and 0 <= r < pc.n_rounds
+        w = written.setdefault((int(o), int(r)), np.zeros(S, np.int8))
+        w[do:do + c] += 1
+        if t >= 0:
+            i = cls.indices[t]
+            assert p.owner[i] == o and cls.offset[i] + so == r * S + do
+            covered[i][so:so + c] += 1
+    assert all((v == 1).all() for v in covered.values())
+    for o in range(world):
+        counts = pc.own_counts(cls, o)
+        assert sum(counts) == cls.own_len[o]
+        for r in range(pc.n_rounds):
+            w = written.get((o, r), np.zeros(S, np.int8))
+            assert (w[:counts[r]] == 1).all() and (w[counts[r]:] == 0).all()
+
+
+@settings(max_examples=100, deadline=None)
+@given(sizes_st, st.integers(min_value=2, max_value=9), rounds_st, st.integers(min_value=0, max_value=4),
+       st.floats(min_value=0.0, max_value=1.0))
+def test_round_push_split_and_landing_pieces_partition(numels, world, units, streams, share):
+    p = layout.plan(numels, [HA_BF16] * len(numels), world)
+    (cls,) = p.classes
+    pc = layout.exchange_pieces(cls, p.owner, numels, units * layout.ALIGN)
+    for rank in range(world):
+        for k in range(pc.n_rounds):
+            kernel, groups = layout.round_push_split(pc, k, rank, streams, share)
+            ce = np.concatenate(groups) if groups else np.zeros(0, np.int64)
+            assert sorted(kernel.tolist() + ce.tolist()) == np.nonzero(pc.round == k)[0].tolist()
+            assert (pc.owner[ce] != rank).all()
+    lp = layout.landing_pieces(pc, len(cls.indices))
+    flat = np.concatenate(lp) if lp else np.zeros(0, np.int64)
+    assert sorted(flat.tolist()) == np.nonzero((pc.round < layout.LAND_ROUNDS) & (pc.tensor >= 0))[0].tolist()
+    for k, idx in enumerate(lp):
+        assert (pc.tensor[idx] == k).all()
+
+
+@settings(max_examples=100, deadline=None)
+@given(st.lists(st.integers(min_value=1, max_value=10**6), max_size=60), st.integers(min_value=1, max_value=8))
+def test_balanced_groups_are_a_partition_within_one_item(sizes, n):
+    entries = np.arange(100, 100 + len(sizes))
+    groups = layout.balanced_groups(entries, np.asarray(sizes, np.int64), n)
+    assert len(groups) == n
+    assert sorted(np.concatenate(groups).tolist()) == entries.tolist()
+    if sizes:
+        loads = [sum(sizes[int(e) - 100] for e in g) for g in groups]
+        assert max(loads) - min(loads) <= max(sizes)
