@@ -40,7 +40,6 @@ import datetime
 import json
 import math
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -53,8 +52,10 @@ sys.path.insert(0, ROOT)
 ALGO_BYTES_ADAMW = {"bf16": 28, "f16": 28, "f32": 28}   # per owned parameter, per AdamW launch
 ALGO_BYTES_SUMSQ = {"bf16": 2, "f16": 2, "f32": 4}
 FALLBACK_HBM_GBS = 6650.0
-NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's B200s (the NVLink roofline reference)
-TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "adamw_kernel_qwen3_8b.md")
+RECIPE_NVLINK_GBS = 770.0   # the pool's published peer-copy figure, used only where no probe of ours exists
+NOMINAL_NVLINK_GBS = 900.0  # NVLink 5, per direction per GPU
+TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "adamw_kernel_qwen3_8b.json")
+LINK_PROFILE = os.path.join(ROOT, "profiles", "nvlink_peak.json")
 
 
 def parse_args():
@@ -71,61 +72,302 @@ def parse_args():
     ap.add_argument("--max-params", type=int, default=0, help="truncate the parameter set (smoke / profiling)")
     ap.add_argument("--landing", action="store_true", help="measure gradient landing (N > 1)")
     ap.add_argument("--tokens", type=int, default=2048, help="tokens of the --landing synthetic backward")
+    ap.add_argument("--probe-links", action="store_true", help="measure NVLink bandwidth between the N GPUs")
+    ap.add_argument("--probe-bytes", type=int, default=2 << 30, help="--probe-links: bytes each rank moves")
+    ap.add_argument("--parity-per-rank", type=int, default=100_000,
+                    help="sampled positions per rank of the checked step after timing (0: no check)")
     ap.add_argument("--land-ctas", default="0,64", help="--landing: comma-separated CTA caps of the early "
                     "pushes to measure (0: copy engines)")
     return ap.parse_args()
 
 
-# ---------------------------------------------------------------- CPU baseline (reference op sequence)
-def cpu_baseline(workload: str, sample_params: int, steps: int = 4, warmup: int = 1) -> dict:
-    """The reference's per-tensor eager op sequence (hybrid_rl/optimizer.py:148-191, as
-    restated op for op in oracle/torch_ops.py) on CPU tensors over the leading tensors of
-    the parameter set, bf16 params / grads with fp32 state at step 100, all host threads."""
+# ---------------------------------------------------------------- CPU baseline / reference arm
+def _reference_class():
+    """The reference's own ``ZeroOneAdamW`` staged unmodified under oracle/_ref by
+    oracle/stage_ref.py (kind "reference"), else the op-for-op restatement of its world-1
+    path in oracle/torch_ops.py (kind "port")."""
+    from oracle import stage_ref
+    if stage_ref.staged() is not None:
+        if stage_ref.OUT not in sys.path:
+            sys.path.insert(0, stage_ref.OUT)
+        from hybrid_rl.optimizer import ZeroOneAdamW
+        return ZeroOneAdamW, "reference"
+    return None, "port"
+
+
+def _world1_gloo() -> None:
+    """A world-size-1 gloo process group, as the north star's CPU baseline specifies (at world 1
+    the reference issues no collective: optimizer.py:99, 152, 168, 192)."""
+    import torch.distributed as dist
+    if not dist.is_initialized():
+        dist.init_process_group("gloo", store=dist.HashStore(), rank=0, world_size=1)
+
+
+def reference_cpu(shapes, dtype, *, lr: float, grad_sigma: float, preload: bool, steps: int, warmup: int,
+                  fresh_grads: bool, seed: int = 7) -> dict:
+    """Times the reference optimizer on CPU tensors at world size 1: per step the caller's
+    gradients are set (outside the timed region) and ``all_reduce_grads() +
+    clip_grad_norm(1.0) + step()`` is timed (hybrid_rl/train.py:287-295), every host thread.
+    ``preload``: m ~N(0,1e-5), v ~|N(0,1e-8)|, step 100 (the GPU arm's state)."""
     import torch
 
-    from hybridagent_b200 import workloads
     from oracle.torch_ops import TorchZeroOneW1
 
-    torch.set_num_threads(len(os.sched_getaffinity(0)))  # every host core (torchrun would leave 1)
-    shapes = workloads.truncated(workloads.WORKLOADS[workload](), sample_params)
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)  # every host core (torchrun would leave 1)
+    cls, kind = _reference_class()
     n = sum(math.prod(s) for s in shapes)
-    g = torch.Generator().manual_seed(7)
-    params = [(torch.randn(s, generator=g) * 0.02).to(torch.bfloat16) for s in shapes]
-    opt = TorchZeroOneW1(params, 1e-6, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
-    for i, s in enumerate(shapes):
-        opt.exp_avg[i].normal_(0, 1e-5, generator=g)
-        opt.exp_avg_sq[i].normal_(0, 1e-8, generator=g).abs_()
-        opt.steps[i] = 100
-    grads = [(torch.randn(s, generator=g) * 1e-4).to(torch.bfloat16) for s in shapes]
-    times = []
+    g = torch.Generator().manual_seed(seed)
+    params = [torch.nn.Parameter((torch.randn(s, generator=g) * 0.02).to(dtype)) for s in shapes]
+    if cls is not None:
+        _world1_gloo()
+        opt = cls([{"params": params, "lr": lr}], rank=0, world_size=1, betas=(0.9, 0.999), eps=1e-8,
+                  weight_decay=0.01)
+        state = [(opt.exp_avg[i], opt.exp_avg_sq[i]) for i in range(len(shapes))]
+    else:
+        opt = TorchZeroOneW1([p.data for p in params], lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+        state = list(zip(opt.exp_avg, opt.exp_avg_sq))
+    if preload:
+        for i, (m, v) in enumerate(state):
+            m.normal_(0, 1e-5, generator=g)
+            v.normal_(0, 1e-8, generator=g).abs_()
+            if cls is not None:
+                opt.param_steps[i] = 100
+            else:
+                opt.steps[i] = 100
+
+    def grads():
+        return [(torch.randn(s, generator=g) * grad_sigma).to(dtype) for s in shapes]
+
+    base = grads()
+    times, norms = [], []
     for k in range(warmup + steps):
-        fresh = [x.clone() for x in grads]  # the step clips its gradients in place
-        t0 = time.perf_counter()
-        opt.step(fresh, 1.0)
+        fresh = grads() if fresh_grads else [x.clone() for x in base]  # the clip scales gradients in place
+        if cls is not None:
+            opt.zero_grad(set_to_none=True)
+            for p, x in zip(params, fresh):
+                p.grad = x
+            t0 = time.perf_counter()
+            opt.all_reduce_grads()
+            norm = opt.clip_grad_norm(1.0)
+            opt.step()
+        else:
+            t0 = time.perf_counter()
+            norm = opt.step(fresh, 1.0)
         dt = time.perf_counter() - t0
         if k >= warmup:
             times.append(dt)
-    sec = statistics.median(times)
+            norms.append(norm)
+    sec = sum(times) / len(times)
     return {"value": round(n / sec / 1e9, 4), "unit": "Gparams/s", "cores": torch.get_num_threads(),
-            "kind": "port", "ms_per_step": round(sec * 1e3, 2),
-            "sample": f"leading {len(shapes)} tensors of {workload} ({n} params), bf16 params/grads, fp32 state; "
-                      f"median of {steps} steps after {warmup} warm-up; torch {torch.__version__} CPU, "
-                      f"{len(os.sched_getaffinity(0))} host CPUs visible"}
+            "kind": kind, "ms_per_step": round(sec * 1e3, 3), "steps": steps, "warmup": warmup, "params": n,
+            "tensors": len(shapes), "last_norm": norms[-1] if norms else None,
+            "impl": ("hybrid_rl.optimizer.ZeroOneAdamW (unmodified, staged by oracle/stage_ref.py), world size 1 "
+                     "over gloo" if kind == "reference" else "oracle/torch_ops.py restatement (reference not staged)"),
+            "host": f"torch {torch.__version__} CPU, {cores} host CPUs visible, {torch.get_num_threads()} threads"}
+
+
+def cpu_sample(workload: str, sample_params: int, steps: int, warmup: int) -> dict:
+    """The reference on CPU over the leading tensors of the GPU arm's parameter set (bf16
+    parameters and gradients, fp32 state pre-loaded at step 100, the same gradients every step)."""
+    import torch
+
+    from hybridagent_b200 import workloads
+    shapes = workloads.truncated(workloads.WORKLOADS[workload](), sample_params)
+    out = reference_cpu(shapes, torch.bfloat16, lr=1e-6, grad_sigma=1e-4, preload=True, steps=steps,
+                        warmup=warmup, fresh_grads=False)
+    out["sample"] = (f"leading {out['tensors']} tensors of {workload} ({out['params']} params), bf16 params/grads, "
+                     f"fp32 state at step 100; mean of {steps} timed steps after {warmup} warm-up; {out['host']}")
+    return out
+
+
+def cpu_config1(steps: int = 9, warmup: int = 1) -> dict:
+    """BASELINE configuration 1 on the reference: 64 fp32 tensors (48 x 256x512, 8 x 1024x256,
+    8 x 65536; 8,912,896 params), params ~N(0,0.02), fresh grads ~N(0,1e-3) every step, m = v =
+    0, lr 1e-6, wd 0.01, clip 1.0, 10 steps of which the first is not timed."""
+    import torch
+
+    from hybridagent_b200 import workloads
+    out = reference_cpu(workloads.config1_cpu(), torch.float32, lr=1e-6, grad_sigma=1e-3, preload=False,
+                        steps=steps, warmup=warmup, fresh_grads=True, seed=11)
+    out["sample"] = (f"BASELINE config 1 in full: {out['params']} fp32 params in 64 tensors, fresh grads each step, "
+                     f"{warmup + steps} steps, the first untimed; {out['host']}")
+    return out
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # one CPU measurement per job, on rank 0
-    base = cpu_baseline(args.workload, args.cpu_sample_params, steps=min(max(args.steps, 1), 4), warmup=1)
+    steps, warmup = max(args.steps, 1), max(args.warmup, 0)
+    base = cpu_sample(args.workload, args.cpu_sample_params, steps=steps, warmup=warmup)
+    cfg1 = cpu_config1()
     out = {"metric": "ZeRO-1 AdamW step Gparams/s", "value": base["value"], "unit": "Gparams/s",
-           "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+           "impl": "reference", "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
            "ms_per_step": base["ms_per_step"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
            "dtype": "fp32", "data": "synthetic",
-           "config": {"workload": args.workload, "sample": base["sample"]},
-           "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+           "config": {"workload": args.workload, "sample": base["sample"], "params_timed": base["params"]},
+           "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample", "impl")},
+           "config1": {k: cfg1[k] for k in ("value", "unit", "ms_per_step", "cores", "kind", "steps", "warmup",
+                                            "params", "sample", "last_norm")},
            "e2e": {"value": base["value"], "unit": "Gparams/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
+
+
+# ---------------------------------------------------------------- sampled parity (after the timed region)
+class SampledParity:
+    """A checked optimizer step over seeded sample positions of the whole parameter set.
+
+    Run once, after timing.  Every rank copies to the host-visible gather its gradients at
+    every sampled position and, at the positions of the tensors it owns, master / exp_avg /
+    exp_avg_sq and the step count before the step, its reduced gradient after
+    ``all_reduce_grads``, and its state after ``step``; every rank also copies its bf16
+    parameters afterwards.  Rank 0 then recomputes the step at those positions with torch's
+    own CUDA kernels running the reference's op sequence (hybrid_rl/optimizer.py:151-191):
+    the owner's sum of the W ranks' gradients (fp32 adds in rank order, one rounding to the
+    gradient dtype: exact at W <= 2, the build's documented reduction at W > 2; the
+    reference's ``dist.reduce`` rounds per hop in NCCL's own order), the clip factor of this
+    step's norm (optimizer.py:156-159), the update and the bf16 copy; every rank's parameter
+    must equal the owner's.  The norm itself is checked against an independent fp64 sum of
+    the reduced gradients.  Nothing here is timed."""
+
+    def __init__(self, numels: list[int], per_rank: int, world: int, seed: int, dev):
+        import numpy as np
+        import torch
+        rng = np.random.default_rng(seed)
+        bounds = np.concatenate([[0], np.cumsum(numels)]).astype(np.int64)
+        flat = rng.integers(0, int(bounds[-1]), size=per_rank * world, dtype=np.int64)
+        # every tensor's first and last element as well (ragged tails, 1-element tensors)
+        flat = np.unique(np.concatenate([flat, bounds[:-1], bounds[1:] - 1]))
+        tensor = np.searchsorted(bounds, flat, side="right") - 1
+        offset = flat - bounds[tensor]
+        self.tensor = tensor
+        self.k = len(flat)
+        self.groups = []
+        for i in np.unique(tensor):
+            sel = tensor == i
+            self.groups.append((int(i), torch.from_numpy(offset[sel]).to(dev)))
+        self.dev = dev
+        self.world = world
+
+    def take(self, get, dtype):
+        """Values at every sample position of the tensors ``get(i)`` returns (zeros where it
+        returns None), concatenated in position order."""
+        import torch
+        parts = []
+        for i, idx in self.groups:
+            t = get(i)
+            parts.append(torch.zeros(len(idx), dtype=dtype, device=self.dev) if t is None
+                         else t.detach().reshape(-1)[idx].to(dtype))
+        return torch.cat(parts)
+
+    def gather(self, x):
+        """[world, k] of every rank's x (raw bits travel unchanged)."""
+        import torch
+        import torch.distributed as dist
+        if self.world == 1:
+            return x[None]
+        raw = x.contiguous().view(torch.uint8)  # bytes: NCCL moves them untouched
+        out = torch.empty((self.world, raw.numel()), dtype=torch.uint8, device=self.dev)
+        dist.all_gather_into_tensor(out.view(-1), raw)
+        return out.view(x.dtype)
+
+
+def _ordered_bits(x):
+    """fp32 bit patterns mapped to integers that order like the values (ulp distances)."""
+    import torch
+    b = x.view(torch.int32).to(torch.int64)
+    return torch.where(b < 0, -(b & 0x7FFFFFFF), b)
+
+
+def checked_step(opt, params, inputs, numels, per_rank: int, max_norm: float = 1.0) -> dict:
+    """One optimizer step with the sampled parity check; returns the bench line's
+    ``parity`` object (on every rank; rank 0's is printed)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world, dev = opt.world, params[0].device
+    sync = torch.cuda.synchronize if dev.type == "cuda" else (lambda: None)
+    sp = SampledParity(numels, per_rank, world, seed=20261202, dev=dev)
+    gdt = params[0].dtype  # the benchmark's sets have one parameter dtype
+    bits = torch.int16 if params[0].element_size() == 2 else torch.int32
+    owner = torch.as_tensor(np.asarray(opt.owner)[sp.tensor], device=dev)
+    owned = set(opt.param_steps)
+    mine = lambda d: (lambda i: d[i] if i in owned else None)  # noqa: E731
+
+    for p, g in zip(params, inputs):
+        p.grad = g
+    sync()
+    g_pre = sp.gather(sp.take(lambda i: params[i].grad, gdt))
+    st_pre = [sp.gather(sp.take(mine(d), torch.float32)) for d in (opt.master, opt.exp_avg, opt.exp_avg_sq)]
+    steps = torch.zeros(len(params), dtype=torch.int64, device=dev)
+    for i in owned:
+        steps[i] = opt.param_steps[i]
+    if world > 1:
+        dist.all_reduce(steps)
+    opt.all_reduce_grads()
+    g_red = sp.gather(sp.take(mine({i: params[i].grad for i in owned}), gdt))
+    # independent norm: fp64 sum of the squares of this rank's reduced gradients, all ranks
+    acc = torch.zeros((), dtype=torch.float64, device=dev)
+    for i in owned:
+        g = params[i].grad
+        if g is not None:
+            for part in g.reshape(-1).split(1 << 26):
+                acc += part.double().square().sum()
+    if world > 1:
+        dist.all_reduce(acc)
+    norm = opt.clip_grad_norm(max_norm)
+    opt.step()
+    sync()
+    st_post = [sp.gather(sp.take(mine(d), torch.float32)) for d in (opt.master, opt.exp_avg, opt.exp_avg_sq)]
+    p_post = sp.gather(sp.take(lambda i: params[i].detach(), gdt))
+
+    # --- expected values, torch CUDA kernels, the reference's op sequence
+    sel = owner[None]
+    pick = lambda a: a.gather(0, sel)[0]  # noqa: E731  the owner's row at every position
+    acc32 = g_pre[0].float()
+    for r in range(1, world):
+        acc32 = acc32 + g_pre[r].float()
+    g_exp = acc32.to(gdt)
+    red_bad = int((pick(g_red).view(bits) != g_exp.view(bits)).sum())
+    exact = math.sqrt(float(acc))
+    g_clip = g_exp.clone()
+    if max_norm > 0 and norm > max_norm:
+        g_clip.mul_(float(max_norm) / (norm + 1e-6))  # optimizer.py:156-159 (bf16 in place)
+    master, m, v = (pick(a).clone() for a in st_pre)
+    t_all = steps[torch.as_tensor(sp.tensor, device=dev)] + 1
+    lr = torch.as_tensor(np.asarray(opt.lrs, dtype=np.float64)[sp.tensor], device=dev)
+    b1, b2 = opt.betas
+    for t in torch.unique(t_all).tolist():
+        for lr_v in torch.unique(lr[t_all == t]).tolist():
+            s = (t_all == t) & (lr == lr_v)
+            gradient = g_clip[s].float()
+            ms, ma, va = master[s], m[s], v[s]
+            c1, c2 = 1.0 - b1 ** t, 1.0 - b2 ** t
+            if opt.weight_decay:
+                ms.mul_(1.0 - lr_v * opt.weight_decay)
+            ma.mul_(b1).add_(gradient, alpha=1.0 - b1)
+            va.mul_(b2).addcmul_(gradient, gradient, value=1.0 - b2)
+            den = (va / c2).sqrt().add_(opt.eps)
+            ms.addcdiv_(ma / c1, den, value=-lr_v)
+            master[s], m[s], v[s] = ms, ma, va
+    p_exp = master.to(gdt)
+    fields = {"reduced_grad": red_bad}
+    max_ulp = 0
+    for name, got, want in (("master", pick(st_post[0]), master), ("exp_avg", pick(st_post[1]), m),
+                            ("exp_avg_sq", pick(st_post[2]), v)):
+        d = (_ordered_bits(got) - _ordered_bits(want)).abs()
+        fields[name] = int((d != 0).sum())
+        max_ulp = max(max_ulp, int(d.max()))
+    fields["param_every_rank"] = int((p_post.view(bits) != p_exp.view(bits)[None]).sum())
+    rel = abs(norm - exact) / exact if exact else abs(norm)
+    return {"checked_positions": sp.k, "checked_values": sp.k * (4 + world), "mismatches": sum(fields.values()),
+            "max_ulp": max_ulp, "fields": fields,
+            "norm": {"returned": norm, "fp64_of_reduced": exact, "rel_err": rel, "ok": bool(rel <= 1e-6)},
+            "reduction": "exact (W<=2)" if world <= 2 else f"fp32 rank-order sum rounded once to {str(gdt)[6:]}",
+            "checker": "torch CUDA ops running the reference's op sequence at seeded positions (plus every "
+                       "tensor's first and last element), after the timed region"}
 
 
 # ---------------------------------------------------------------- GPU helpers
@@ -220,13 +462,29 @@ def measured_hbm_peak() -> tuple[float, str]:
 
 
 def profiled_traffic_per_param() -> float | None:
-    """DRAM bytes per owned parameter of one AdamW launch, from the committed ncu summary."""
+    """DRAM bytes per owned parameter of one AdamW launch, from the committed ncu record."""
     try:
-        text = open(TRAFFIC_PROFILE).read()
-    except OSError:
+        with open(TRAFFIC_PROFILE) as f:
+            return float(json.load(f)["traffic_bytes_per_param"])
+    except (OSError, KeyError, ValueError):
         return None
-    m = re.search(r"traffic_bytes_per_param:\s*([0-9.]+)", text)
-    return float(m.group(1)) if m else None
+
+
+def measured_link_peak(world: int) -> tuple[float, str]:
+    """Per-direction NVLink bandwidth at this world size: the best pattern of the committed
+    ``bench.py --probe-links`` record at that size (or the nearest size probed), else the
+    pool's published peer-copy figure."""
+    try:
+        with open(LINK_PROFILE) as f:
+            by_world = json.load(f)["by_world"]
+    except (OSError, KeyError, ValueError):
+        return RECIPE_NVLINK_GBS, "recipe figure (no probe record)"
+    sizes = sorted(int(k) for k in by_world)
+    if not sizes:
+        return RECIPE_NVLINK_GBS, "recipe figure (no probe record)"
+    w = min(sizes, key=lambda s: (abs(s - world), -s))
+    best = max(by_world[str(w)].items(), key=lambda kv: kv[1])
+    return float(best[1]), f"measured: profiles/nvlink_peak.json, world {w}, {best[0]}"
 
 
 def run_ours(args) -> None:
@@ -252,21 +510,25 @@ def run_ours(args) -> None:
     numels = [math.prod(s) for s in shapes]
     n_params = sum(numels)
 
-    # parameters (identical on every rank), bf16, ~N(0, 0.02)
+    # BASELINE config 1 is fp32 throughout with grads ~N(0,1e-3) and fresh state; the model-shaped
+    # sets are bf16 with grads ~N(0,1e-4) and state pre-loaded at step 100
+    fp32_set = args.workload == "config1_cpu"
+    pdt = torch.float32 if fp32_set else torch.bfloat16
+    # parameters (identical on every rank), ~N(0, 0.02)
     gen = torch.Generator(device=dev).manual_seed(1234)
-    params = [torch.nn.Parameter((torch.randn(s, device=dev, generator=gen) * 0.02).to(torch.bfloat16))
-              for s in shapes]
+    params = [torch.nn.Parameter((torch.randn(s, device=dev, generator=gen) * 0.02).to(pdt)) for s in shapes]
     opt = ZeroOneAdamW([{"params": params, "lr": 1e-6}], rank=rank, world_size=world, betas=(0.9, 0.999), eps=1e-8,
                        weight_decay=0.01)
-    # state pre-loaded at step 100: m ~N(0,1e-5), v ~|N(0,1e-8)|
-    gs = torch.Generator(device=dev).manual_seed(99 + rank)
-    for i in opt.param_steps:
-        opt.exp_avg[i].normal_(0, 1e-5, generator=gs)
-        opt.exp_avg_sq[i].normal_(0, 1e-8, generator=gs).abs_()
-        opt.param_steps[i] = 100
-    # this rank's gradients of the whole model, ~N(0, 1e-4) bf16 (different per rank)
+    if not fp32_set:  # state pre-loaded at step 100: m ~N(0,1e-5), v ~|N(0,1e-8)|
+        gs = torch.Generator(device=dev).manual_seed(99 + rank)
+        for i in opt.param_steps:
+            opt.exp_avg[i].normal_(0, 1e-5, generator=gs)
+            opt.exp_avg_sq[i].normal_(0, 1e-8, generator=gs).abs_()
+            opt.param_steps[i] = 100
+    # this rank's gradients of the whole model (different per rank)
     gg = torch.Generator(device=dev).manual_seed(555 + rank)
-    inputs = [(torch.randn(s, device=dev, generator=gg) * 1e-4).to(torch.bfloat16) for s in shapes]
+    sigma = 1e-3 if fp32_set else 1e-4
+    inputs = [(torch.randn(s, device=dev, generator=gg) * sigma).to(pdt) for s in shapes]
     owned = list(opt.param_steps)
     owned_params = sum(numels[i] for i in owned)
     torch.cuda.synchronize()
@@ -316,9 +578,9 @@ def run_ours(args) -> None:
     e2e = None
     if not args.no_e2e:
         pool_elems = min(max(numels), 1 << 31)
-        host = torch.empty(pool_elems, dtype=torch.bfloat16, pin_memory=True)
+        host = torch.empty(pool_elems, dtype=pdt, pin_memory=True)
         host.copy_(inputs[int(np.argmax(numels))].reshape(-1)[:pool_elems].cpu())
-        h2d_bytes = 2 * n_params
+        h2d_bytes = inputs[0].element_size() * n_params
         d2h_bytes = 8 * len(opt._classes)
 
         # double-buffered inputs: step k+1's gradients cross PCIe on a copy stream while step
@@ -378,9 +640,15 @@ def run_ours(args) -> None:
                       f"memory (per-tensor cudaMemcpyAsync, {how}) and reads the norm back in clip_grad_norm"}
         del spare, bufs
 
+    # ---- one more step, checked at sampled positions against torch's CUDA kernels (not timed)
+    parity = None
+    if args.parity_per_rank > 0:
+        parity = checked_step(opt, params, inputs, numels, args.parity_per_rank)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(args.workload, args.cpu_sample_params)
+        base = cpu_sample(args.workload, args.cpu_sample_params, steps=4, warmup=1)
+        cpu = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample", "impl", "ms_per_step")}
 
     if rank != 0:
         if world > 1:
@@ -393,23 +661,51 @@ def run_ours(args) -> None:
     algo = ALGO_BYTES_ADAMW["bf16"] * owned_params
     achieved = algo / (adamw_ms * 1e-3) / 1e9 if adamw_ms else None
     tpp = profiled_traffic_per_param()
-    nvlink = None
+    hbm_roof = {"bound": "hbm", "kernel": f"adamw_kernel<{'f32' if fp32_set else 'bf16'}>",
+                "achieved": None if achieved is None else round(achieved, 1),
+                "peak": peak, "unit": "GB/s",
+                "frac": None if achieved is None else round(achieved / peak, 4),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                else "fallback 6.65 TB/s",
+                "algorithmic_bytes_per_launch": algo,
+                "traffic": None if tpp is None else round(tpp * owned_params),
+                "traffic_source": None if tpp is None else "ncu dram__bytes_read+write per parameter of one launch "
+                "(profiles/adamw_kernel_qwen3_8b.json), times this launch's parameters"}
+    roofline, nvlink = hbm_roof, None
     if world > 1 and opt.comm_mode == "p2p":
-        # fused compute + collective kernels: target time = max(HBM bytes / HBM peak, NVLink bytes / link)
-        foreign = n_params - owned_params  # gradients this rank sends, parameters it receives
+        # data crossing NVLink per step and GPU: the gradients this rank sends to their owners and
+        # the parameters it receives ((W-1)/W of 2 B/param each way); target time of a phase =
+        # max(its HBM bytes / HBM peak, its NVLink bytes / link peak)
+        link, link_src = measured_link_peak(world)
+        foreign = n_params - owned_params
         push_link = 2 * foreign
         adamw_link = 2 * owned_params * (world - 1)
-        nvlink = {}
-        for name, link_bytes, hbm_bytes in (("push", push_link, 4 * n_params),
-                                            ("adamw", adamw_link, algo + 2 * foreign)):
+        push_how = ("copy engines, one stream per peer" if opt.push_streams < 0 else
+                    f"copy engines on {opt.push_streams} streams + gather_kernel" if opt.push_streams > 0 else
+                    "gather_kernel peer stores")
+        gather_how = ("adamw_kernel<bf16> in parts + copy-engine all-gather" if opt.gather_mode == "ce"
+                      else "adamw_kernel<bf16, PEERS> (peer stores fused)")
+        nvlink = {"link_peak_gbs": link, "link_peak_source": link_src, "nominal_gbs": NOMINAL_NVLINK_GBS}
+        for name, how, link_bytes, hbm_bytes in (("push", push_how, push_link, 4 * n_params),
+                                                 ("adamw", gather_how, adamw_link, algo + 2 * foreign)):
             ms_phase = phases.get(name)
             if not ms_phase:
                 continue
-            target = max(hbm_bytes / (peak * 1e9), link_bytes / (NVLINK_GBS * 1e9)) * 1e3
-            nvlink[name] = {"measured_ms": round(ms_phase, 3), "target_ms": round(target, 3),
+            target = max(hbm_bytes / (peak * 1e9), link_bytes / (link * 1e9)) * 1e3
+            gbs = link_bytes / (ms_phase * 1e-3) / 1e9
+            nvlink[name] = {"how": how, "measured_ms": round(ms_phase, 3), "target_ms": round(target, 3),
                             "frac": round(target / ms_phase, 4), "nvlink_bytes": link_bytes, "hbm_bytes": hbm_bytes,
-                            "link_gbs_achieved": round(link_bytes / (ms_phase * 1e-3) / 1e9, 1)}
-        nvlink["link_peak"] = f"{NVLINK_GBS} GB/s per direction (measured peer copy)"
+                            "link_gbs_achieved": round(gbs, 1), "frac_of_link_peak": round(gbs / link, 4),
+                            "frac_of_nominal": round(gbs / NOMINAL_NVLINK_GBS, 4)}
+        dom = max((k for k in ("push", "adamw") if k in nvlink), key=lambda k: nvlink[k]["measured_ms"], default=None)
+        if dom is not None:
+            d = nvlink[dom]
+            roofline = {"bound": "nvlink", "kernel": d["how"], "phase": dom, "achieved": d["link_gbs_achieved"],
+                        "peak": link, "unit": "GB/s", "frac": d["frac_of_link_peak"],
+                        "frac_of_nominal": d["frac_of_nominal"], "peak_source": link_src,
+                        "algorithmic_bytes_per_launch": d["nvlink_bytes"], "traffic": None,
+                        "traffic_source": "NVLink bytes are algorithmic; ncu's NVLink counters were not readable "
+                                          "on this pool", "hbm_adamw": hbm_roof}
     out = {
         "metric": "ZeRO-1 AdamW step Gparams/s",
         "value": round(n_params / (ms_max * 1e-3) / 1e9, 3),
@@ -424,23 +720,18 @@ def run_ours(args) -> None:
         "dtype": "fp32",
         "data": "synthetic",
         "config": {"workload": args.workload, "params": n_params, "tensors": len(shapes),
-                   "param_dtype": "bf16", "state_dtype": "fp32", "parallelism": f"zero1_dp{world}",
-                   "l2": f"inputs larger than L2: {(n_params * 16) / 1e9 / world:.0f} GB of grads+state per GPU "
+                   "param_dtype": "fp32" if fp32_set else "bf16", "state_dtype": "fp32",
+                   "parallelism": f"zero1_dp{world}",
+                   "push": push_how if world > 1 and nvlink else None,
+                   "all_gather": gather_how if world > 1 and nvlink else None,
+                   "l2": f"inputs larger than L2: {(n_params * 16) / 1e9 / world:.1f} GB of grads+state per GPU "
                          "per step vs 126 MB L2, no flush"},
-        "roofline": {"bound": "hbm", "kernel": "adamw_kernel<bf16>",
-                     "achieved": None if achieved is None else round(achieved, 1),
-                     "peak": peak, "unit": "GB/s",
-                     "frac": None if achieved is None else round(achieved / peak, 4),
-                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                     else "fallback 6.65 TB/s",
-                     "algorithmic_bytes_per_launch": algo,
-                     "traffic": None if tpp is None else round(tpp * owned_params),
-                     "traffic_source": None if tpp is None else "ncu dram__bytes_read+write per launch, "
-                     "profiles/adamw_kernel_qwen3_8b.md, scaled to this launch's parameters"},
+        "roofline": roofline,
         "phases_ms": {k: round(v, 4) for k, v in phases.items()},
         "comm_mode": opt.comm_mode,
         "roofline_fused": nvlink,
         "last_norm": norm,
+        "parity": parity,
         "cpu_baseline": cpu,
         "e2e": e2e,
         "clocks": clock,
@@ -546,10 +837,132 @@ def run_landing(args) -> None:
     dist.destroy_process_group()
 
 
+def run_probe_links(args) -> None:
+    """NVLink per-direction bandwidth between this node's GPUs, measured the ways the step
+    moves data (one JSON line from rank 0; the figures behind the link roofline).
+
+    Every rank moves ``--probe-bytes`` at once (all ranks together, CUDA events on every
+    stream used, max over ranks, best of ``--steps``), into IPC-mapped buffers of its peers:
+      ce_one_peer   one cudaMemcpyAsync to the next rank (ring);
+      ce_all_peers  1/(W-1) of the bytes to every peer, one copy-engine stream per peer;
+      ce_pull_all   the same bytes read from every peer by the copy engines;
+      sm_one_peer   the library's copy kernel (ha_gather) storing to the next rank;
+      sm_all_peers  the copy kernel storing 1/(W-1) to every peer (one launch, chunks interleaved);
+      sm_pull_all   the copy kernel loading 1/(W-1) from every peer into local memory.
+    Plain loads, stores and copies only (no TMA, no multicast)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from hybridagent_b200 import _lib, layout
+    from hybridagent_b200.p2p import DeviceBuffer, PeerMap
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world < 2 or world != args.gpus:
+        raise SystemExit("--probe-links needs --gpus N > 1 under torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    total = args.probe_bytes // (2 * (world - 1) * 256) * (2 * (world - 1) * 256)  # whole 16-byte vectors per peer
+    per_peer = total // (world - 1)
+    src = DeviceBuffer(total // 2, torch.bfloat16, dev)
+    src.tensor.view(torch.int16).copy_(torch.arange(total // 2, device=dev, dtype=torch.int32).to(torch.int16))
+    recv = DeviceBuffer(world * total // 2, torch.bfloat16, dev)  # region r: what rank r sent here
+    pm = PeerMap({"src": src, "recv": recv}, rank, world)
+    if not pm.ok:
+        raise SystemExit(f"peer mapping failed: {pm.error}")
+    nxt = (rank + 1) % world
+    peers = [(rank + 1 + j) % world for j in range(world - 1)]
+    streams = [torch.cuda.Stream(device=dev) for _ in peers]
+    main = torch.cuda.current_stream()
+
+    def entries(kind: str) -> list[tuple[int, int, int]]:
+        """(src address, dst address, bytes) of this rank's copies for a pattern."""
+        if kind == "one":
+            return [(src.ptr, pm.bases["recv"][nxt] + rank * total, total)]
+        if kind == "push":
+            return [(src.ptr + j * per_peer, pm.bases["recv"][q] + rank * total + j * per_peer, per_peer)
+                    for j, q in enumerate(peers)]
+        # pull: peer q's slice j of its source into region q of this rank's own buffer
+        return [(pm.bases["src"][q] + j * per_peer, recv.ptr + q * total + j * per_peer, per_peer)
+                for j, q in enumerate(peers)]
+
+    def table(ents):
+        t = np.zeros(len(ents), dtype=_lib.COPY_DTYPE)
+        for k, (a, b, n) in enumerate(ents):
+            t[k]["src"], t[k]["dst"], t[k]["numel"] = a, b, n // 2
+        return t
+
+    def run_ce(ents):
+        ready = torch.cuda.Event()
+        ready.record(main)
+        for st, e in zip(streams, ents):
+            st.wait_event(ready)
+            _lib.call("ha_copy_async", _lib.np_ptr(table([e])), 1, 2, st.cuda_stream)
+        for st in streams[:len(ents)]:
+            main.wait_stream(st)
+
+    sm_tabs = {}
+
+    def run_sm(kind):
+        if kind not in sm_tabs:
+            ents = entries(kind)
+            t = table(ents)
+            counts = t["numel"].astype(np.int64)
+            ch = layout.interleaved_chunks(np.arange(len(ents)), np.arange(len(ents)), counts, 0, len(ents),
+                                           _lib.HA_ADAMW_CHUNK)
+            sm_tabs[kind] = (torch.from_numpy(t.view(np.uint8).copy()).to(dev),
+                             torch.from_numpy(ch.view(np.uint8).copy()).to(dev), len(ch))
+        t, ch, n = sm_tabs[kind]
+        _lib.call("ha_gather", t.data_ptr(), ch.data_ptr(), n, _lib.HA_ADAMW_CHUNK, 2, main.cuda_stream)
+
+    patterns = {"ce_one_peer": lambda: run_ce(entries("one")), "ce_all_peers": lambda: run_ce(entries("push")),
+                "ce_pull_all": lambda: run_ce(entries("pull")), "sm_one_peer": lambda: run_sm("one"),
+                "sm_all_peers": lambda: run_sm("push"), "sm_pull_all": lambda: run_sm("pull")}
+    results = {}
+    for name, fn in patterns.items():
+        best = None
+        for it in range(max(args.warmup, 1) + max(args.steps, 1)):
+            dist.barrier()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(main)
+            fn()
+            b.record(main)
+            torch.cuda.synchronize()
+            t = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            if it >= max(args.warmup, 1):
+                best = float(t) if best is None else min(best, float(t))
+        results[name] = {"ms": round(best, 4), "gbs_per_direction": round(total / (best * 1e-3) / 1e9, 1)}
+    # the last pattern wrote region q of this rank's buffer from peer q's source: check the bytes
+    dist.barrier()
+    got, want = recv.tensor.view(torch.int16), src.tensor.view(torch.int16)
+    ok = all(torch.equal(got[q * total // 2 + j * per_peer // 2:q * total // 2 + (j + 1) * per_peer // 2],
+                         want[j * per_peer // 2:(j + 1) * per_peer // 2]) for j, q in enumerate(peers))
+    flag = torch.tensor([0 if ok else 1], device=dev)
+    dist.all_reduce(flag)
+    if rank == 0:
+        print(json.dumps({"probe": "nvlink", "n_gpus": world, "bytes_per_rank": total, "steps": args.steps,
+                          "warmup": args.warmup, "data_ok": int(flag) == 0, "results": results,
+                          "how": "every rank at once, CUDA events on the launching stream (copy streams joined), "
+                                 "max over ranks, best of the timed repetitions; bytes = this rank's egress "
+                                 "(ingress for the pulls)"}), flush=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    pm.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.probe_links:
+        run_probe_links(args)
     elif args.landing:
         run_landing(args)
     else:

@@ -250,19 +250,62 @@ def balanced_groups(entries: np.ndarray, sizes: np.ndarray, n: int) -> list[np.n
     return [np.asarray(entries, dtype=np.int64)[sorted(g)] for g in groups]
 
 
+def peer_groups(entries: np.ndarray, entry_owner: np.ndarray, rank: int, world: int) -> list[np.ndarray]:
+    """``entries`` bound for peers grouped by destination: group j holds those owned by rank
+    (rank + 1 + j) % world, in their original order (world - 1 groups).  One copy-engine
+    stream per group keeps every peer's ingress fed from every rank at once."""
+    owners = np.asarray(entry_owner)[entries] if len(entries) else np.zeros(0, dtype=np.int64)
+    return [np.asarray(entries, dtype=np.int64)[owners == (rank + 1 + j) % world] for j in range(world - 1)]
+
+
 def round_push_split(pc: Pieces, k: int, rank: int, push_streams: int,
-                     kernel_share: float) -> tuple[np.ndarray, list[np.ndarray]]:
+                     kernel_share: float, world: int = 0) -> tuple[np.ndarray, list[np.ndarray]]:
     """Round k's pieces split between the push kernel and the copy engines.  With
     ``push_streams`` 0 the kernel pushes every piece; otherwise it takes this rank's own
     pieces and the smallest peer-bound ones (``kernel_share`` of their bytes), and the rest
-    go to ``push_streams`` copy-engine groups of about equal bytes."""
+    go to the copy engines: ``push_streams`` > 0 groups of about equal bytes, or (-1) one
+    group per destination peer (``peer_groups``, needs ``world``)."""
     entries = np.nonzero(pc.round == k)[0]
-    if push_streams <= 0:
+    if push_streams == 0:
         return entries, []
     remote = entries[pc.owner[entries] != rank]
     remote, by_kernel = split_smallest(remote, pc.count[remote], kernel_share)
     kernel = np.sort(np.concatenate([entries[pc.owner[entries] == rank], by_kernel]))
+    if push_streams < 0:
+        return kernel, peer_groups(np.sort(remote), pc.owner, rank, world)
     return kernel, balanced_groups(remote, pc.count[remote], push_streams)
+
+
+def gather_parts(chunks: np.ndarray, offsets: list[int], numels: list[int], chunk_elems: int,
+                 part_elems: int) -> list[tuple[int, int, int, int]]:
+    """The owned segment's update cut into parts for the copy-engine parameter all-gather.
+
+    ``chunks`` is the update's ha_chunk list over the owned tensors (entry k: slot offset
+    ``offsets[k]`` in the owner's segment, ``numels[k]`` elements).  Returns (first chunk,
+    chunk count, first element, end element) per part, each part about ``part_elems``
+    elements of the segment: updating part j and copying its elements [first, end) to the
+    peers can start as soon as part j's chunks are done, while part j + 1 updates.  Parts
+    cover the segment from its first slot to the end of its last, gaps included (the gaps
+    hold nothing anyone reads), and never split a chunk."""
+    n = len(chunks)
+    if n == 0:
+        return []
+    t = chunks["tensor"].astype(np.int64)
+    j = chunks["index"].astype(np.int64)
+    off = np.asarray(offsets, dtype=np.int64)[t]
+    num = np.asarray(numels, dtype=np.int64)[t]
+    start = off + j * chunk_elems
+    end = off + np.minimum((j + 1) * chunk_elems, num)
+    if np.any(start[1:] < end[:-1]):
+        raise ValueError("gather_parts: chunks are not in segment order")
+    parts, c0 = [], 0
+    while c0 < n:
+        # the last chunk whose end stays within part_elems of this part's start (at least one)
+        c1 = int(np.searchsorted(end, start[c0] + max(part_elems, 1), side="right"))
+        c1 = max(c1, c0 + 1)
+        parts.append((c0, c1 - c0, int(start[c0]), int(end[c1 - 1])))
+        c0 = c1
+    return parts
 
 
 def landing_batch(src: np.ndarray, dst: np.ndarray, count: np.ndarray, chunk_elems: int) -> tuple[np.ndarray, np.ndarray]:

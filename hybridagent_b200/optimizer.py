@@ -246,7 +246,7 @@ class _Class:
             # rank's own pieces only) and the copy-engine groups of the pieces bound for peers
             self.round_chunks, self.round_remote = [], []
             for k in range(pc.n_rounds):
-                entries, groups = layout.round_push_split(pc, k, r, opt.push_streams, opt.push_kernel_share)
+                entries, groups = layout.round_push_split(pc, k, r, opt.push_streams, opt.push_kernel_share, W)
                 self.round_remote.append(groups)
                 tab = layout.interleaved_chunks(entries, pc.owner, pc.count, r, W, HA_ADAMW_CHUNK)
                 _lib.call("ha_check_chunks", len(pc.count), _lib.np_ptr(np.ascontiguousarray(pc.count)),
@@ -265,6 +265,25 @@ class _Class:
             for q, d in enumerate(deltas):
                 self.peers.delta[q] = d
             self.peers.n = len(deltas)
+            # copy-engine all-gather: per part of the update, one copy per peer of the part's
+            # elements of this rank's segment to the same place in the peer's buffer
+            self.gather_parts, self.gather_copies = [], []
+            if opt.gather_mode == "ce" and self.adamw_chunks[1]:
+                tab = layout.chunk_table([numel[i] for i in self.owned], HA_ADAMW_CHUNK)
+                self.gather_parts = layout.gather_parts(tab, [cls.offset[i] for i in self.owned],
+                                                        [numel[i] for i in self.owned], HA_ADAMW_CHUNK,
+                                                        max(opt.gather_part_bytes // esz, HA_ADAMW_CHUNK))
+                seg = param_bases[r] + r * cls.seg_len * esz
+                for _, _, e0, e1 in self.gather_parts:
+                    per_peer = []
+                    for j in range(W - 1):  # peer (r + 1 + j) % W first: every peer's ingress busy at once
+                        q = (r + 1 + j) % W
+                        cp = np.zeros(1, dtype=_lib.COPY_DTYPE)
+                        cp["src"] = seg + e0 * esz
+                        cp["dst"] = param_bases[q] - param_bases[r] + seg + e0 * esz
+                        cp["numel"] = e1 - e0
+                        per_peer.append(cp)
+                    self.gather_copies.append(per_peer)
         else:
             self.recv_buf = None  # not used without peer mappings
             self.grad_buf = torch.zeros(W * cls.seg_len, dtype=self.dtype, device=dev)
@@ -349,6 +368,8 @@ class ZeroOneAdamW:
             self._comm = None
             self._peer_map = None
             self.comm_mode = "local"
+            self.gather_mode = "kernel"
+            self._gather_streams: list = []
             if self.world > 1:
                 from .comm import NcclComm
                 self._comm = NcclComm(self.rank, self.world, timeout_s=comm_timeout_s)
@@ -388,11 +409,20 @@ class ZeroOneAdamW:
         # world 2 (Qwen3-8B set): 33.0 ms per step against 36.2 with the kernel push, whose remote
         # stores need nearly every SM and starve the owner sums; the copy engines move 669 GB/s.
         # At world > 2 this rank's own share and the sums shrink as 1/W: the kernel push stays.
-        self.push_streams = int(os.environ.get("HYBRIDAGENT_B200_PUSH_STREAMS", "2" if self.world == 2 else "0"))
+        push = os.environ.get("HYBRIDAGENT_B200_PUSH_STREAMS", "2" if self.world == 2 else "0")
+        self.push_streams = -1 if push == "peer" else int(push)  # "peer": one copy-engine stream per peer
         # with the copy-engine push: the share of the peer-bound bytes (smallest pieces first) that
         # the push kernel stores instead, using SM time the local copies and sums leave idle and
         # link bandwidth the copy engines leave unused (world 2: 0.1 -> 32.4 ms, 0 -> 33.0, 0.2 -> 32.7)
         self.push_kernel_share = float(os.environ.get("HYBRIDAGENT_B200_PUSH_KERNEL_SHARE", "0.1"))
+        # the parameter all-gather (p2p): "kernel" -- the update kernel stores every new value into
+        # every peer's copy; "ce" -- the update runs in parts of HYBRIDAGENT_B200_GATHER_PART_BYTES and
+        # the copy engines send each finished part to every peer (one stream per peer) while the
+        # next part updates, so the SMs issue no remote store
+        self.gather_mode = os.environ.get("HYBRIDAGENT_B200_GATHER", "kernel")
+        if self.gather_mode not in ("kernel", "ce"):
+            raise ValueError(f"HYBRIDAGENT_B200_GATHER={self.gather_mode!r}: expected kernel or ce")
+        self.gather_part_bytes = int(os.environ.get("HYBRIDAGENT_B200_GATHER_PART_BYTES", str(128 << 20)))
         want = os.environ.get("HYBRIDAGENT_B200_COMM", "p2p")
         if want not in ("p2p", "nccl"):
             raise ValueError(f"HYBRIDAGENT_B200_COMM={want!r}: expected p2p or nccl")
@@ -420,7 +450,10 @@ class ZeroOneAdamW:
                 c.set_mode(self, None, None)
             c.move.upload()
         self._sum_stream = torch.cuda.Stream(device=self.device) if use_p2p else None
-        self._push_streams = [torch.cuda.Stream(device=self.device) for _ in range(self.push_streams)] if use_p2p else []
+        n_push = self.world - 1 if self.push_streams < 0 else self.push_streams
+        self._push_streams = [torch.cuda.Stream(device=self.device) for _ in range(n_push)] if use_p2p else []
+        self._gather_streams = ([torch.cuda.Stream(device=self.device) for _ in range(self.world - 1)]
+                                if use_p2p and self.gather_mode == "ce" else [])
         rounds = max(c.pieces.n_rounds for c in self._classes) if use_p2p else 1
         self._norm_rounds = torch.zeros((len(self._classes), rounds), dtype=torch.float64, device=self.device)
         self._norm_rounds_host = torch.zeros((len(self._classes), rounds), dtype=torch.float64, pin_memory=True)
@@ -879,9 +912,22 @@ class ZeroOneAdamW:
                 launches.append((c, sc))
             p2p = self.comm_mode == "p2p"
             self._phase("adamw", True)
+            ce_gather = p2p and self.gather_mode == "ce"
+            main = torch.cuda.current_stream()
             for c, sc in launches:
                 chunks, n = c.adamw_chunks
-                if n and p2p:  # the update also writes each new parameter into every peer's copy
+                if n and ce_gather:  # update in parts; the copy engines send each finished part to the peers
+                    esz = c.packed_param.element_size()
+                    for (c0, nc, _, _), copies in zip(c.gather_parts, c.gather_copies):
+                        _lib.call("ha_adamw_step", c.table.ptr, chunks.data_ptr() + c0 * _lib.CHUNK_DTYPE.itemsize,
+                                  nc, HA_ADAMW_CHUNK, c.code, c.code, ctypes.byref(sc), main.cuda_stream)
+                        self.launches += 1
+                        done = torch.cuda.Event()
+                        done.record(main)
+                        for st, cp in zip(self._gather_streams, copies):
+                            st.wait_event(done)
+                            _lib.call("ha_copy_async", _lib.np_ptr(cp), 1, esz, st.cuda_stream)
+                elif n and p2p:  # the update also writes each new parameter into every peer's copy
                     _lib.call("ha_adamw_step_peers", c.table.ptr, chunks.data_ptr(), n, HA_ADAMW_CHUNK, c.code,
                               c.code, ctypes.byref(sc), ctypes.byref(c.peers), self._stream())
                     self.launches += 1
@@ -889,6 +935,8 @@ class ZeroOneAdamW:
                     _lib.call("ha_adamw_step", c.table.ptr, chunks.data_ptr(), n, HA_ADAMW_CHUNK, c.code, c.code,
                               ctypes.byref(sc), self._stream())
                     self.launches += 1
+            for st in self._gather_streams:
+                main.wait_stream(st)
             self._phase("adamw", False)
             if p2p:
                 self._phase("barrier", True)

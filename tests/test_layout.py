@@ -1,5 +1,6 @@
 """Owner-major shard layout: slots are aligned, disjoint, inside their owner's segment,
 and cost little padding on the benchmark parameter sets."""
+import numpy as np
 import pytest
 
 from hybridagent_b200 import layout, workloads
@@ -273,3 +274,40 @@ def test_round_push_split_partitions_every_round(world, streams, share):
             if len(by_kernel) and len(ce):
                 assert pc.count[by_kernel].max() <= pc.count[ce].min()  # the smallest ones
 
+
+
+@pytest.mark.parametrize("part", [1, 16384, 50000, 10 ** 9])
+def test_gather_parts_cover_the_owned_segment_in_order(part):
+    """Copy-engine all-gather parts: consecutive chunk ranges, element ranges that start where
+    the previous part ended (or at a later slot) and contain every element of their chunks."""
+    numels = [100000, 7, 40000, 16384, 1, 65536 * 3 + 5]
+    offsets = []
+    o = 0
+    for n in numels:
+        offsets.append(o)
+        o += layout.align_up(n)
+    ch = layout.chunk_table(numels, 16384)
+    parts = layout.gather_parts(ch, offsets, numels, 16384, part)
+    assert parts[0][0] == 0 and sum(p[1] for p in parts) == len(ch)
+    covered = np.zeros(o, dtype=bool)
+    for (c0, nc, e0, e1), nxt in zip(parts, parts[1:] + [None]):
+        assert e0 < e1
+        if nxt is not None:
+            assert nxt[0] == c0 + nc and nxt[2] >= e1
+        assert nc == 1 or e1 - e0 <= max(part, 1)
+        for q in range(c0, c0 + nc):
+            k, j = int(ch[q]["tensor"]), int(ch[q]["index"])
+            a = offsets[k] + j * 16384
+            b = offsets[k] + min((j + 1) * 16384, numels[k])
+            assert e0 <= a and b <= e1
+            covered[a:b] = True
+    for k, n in enumerate(numels):
+        assert covered[offsets[k]:offsets[k] + n].all()
+
+
+def test_peer_groups_one_destination_per_stream():
+    owners = np.array([0, 1, 2, 3, 1, 2, 0, 3])
+    groups = layout.peer_groups(np.array([1, 2, 3, 4, 5, 7]), owners, rank=0, world=4)
+    assert [g.tolist() for g in groups] == [[1, 4], [2, 5], [3, 7]]
+    groups = layout.peer_groups(np.array([0, 2, 6]), owners, rank=2, world=4)
+    assert [g.tolist() for g in groups] == [[], [0, 6], []]

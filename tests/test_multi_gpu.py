@@ -1,7 +1,8 @@
 """The optimizer at world size 2 on two GPUs (skipped with fewer GPUs), in both
 communication modes: p2p (gradients pushed into the owners' buffers over NVLink, summed by
-the owner; parameters stored into every peer by the update kernel) and nccl (local pack,
-NCCL reduce-scatter and all-gather).
+the owner; parameters stored into every peer by the update kernel, or sent by the copy
+engines part by part as the update finishes them) and nccl (local pack, NCCL reduce-scatter
+and all-gather).
 
 Each rank runs tests/world_worker.py under torchrun on a world-size-2 golden case.  At
 world size 2 every reduction's sums have one rounding whatever the algorithm, so the
@@ -32,7 +33,8 @@ def _gpus() -> int:
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("mode", ["p2p", "p2p_rounds", "nccl", "p2p_landing", "p2p_rounds_landing",
-                                  "p2p_landing_copyengine", "p2p_cepush", "p2p_rounds_cepush"])
+                                  "p2p_landing_copyengine", "p2p_cepush", "p2p_rounds_cepush", "p2p_cegather",
+                                  "p2p_rounds_peerpush_cegather"])
 @pytest.mark.parametrize("name", ["bf16_world2", "fp32_world2", "bf16_world2_inf"])
 def test_world2_matches_oracle_and_reference(name, mode, tmp_path):
     """*_landing*: gradients produced by two backward passes and pushed while they land
@@ -43,7 +45,10 @@ def test_world2_matches_oracle_and_reference(name, mode, tmp_path):
         env["HYBRIDAGENT_B200_RECV_BYTES"] = "16384"
     # the peer-bound pieces by the copy engines on 2 streams (the world-2 default: *_cepush and
     # the landing modes) or by the push kernel (p2p, p2p_rounds)
-    env["HYBRIDAGENT_B200_PUSH_STREAMS"] = "2" if ("cepush" in mode or "landing" in mode) else "0"
+    env["HYBRIDAGENT_B200_PUSH_STREAMS"] = ("peer" if "peerpush" in mode else
+                                            "2" if ("cepush" in mode or "landing" in mode) else "0")
+    if "cegather" in mode:  # the update in one-chunk parts, each sent to the peer by the copy engines
+        env.update(HYBRIDAGENT_B200_GATHER="ce", HYBRIDAGENT_B200_GATHER_PART_BYTES="4096")
     if "landing" in mode:
         env.update(WORKER_LANDING="1", HYBRIDAGENT_B200_LAND_BUCKET_BYTES="4096",
                    HYBRIDAGENT_B200_LAND_CTAS="0" if "copyengine" in mode else "3")

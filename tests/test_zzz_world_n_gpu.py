@@ -1,7 +1,7 @@
 """The optimizer at world size 4 and 8 (each skipped without that many GPUs), p2p mode, over
 the bf16_world2 golden case's shapes and seeded gradients on W ranks, with a 16 KiB receive
-window (several exchange rounds), by the push kernel (the default above W = 2) and by the copy
-engines.
+window (several exchange rounds), by the push kernel and by the copy engines (two balanced
+streams, or one stream per peer with the parameter all-gather by the copy engines too).
 
 At W > 2 no two reductions round alike, so the reference is the oracle's W-rank run with the
 owner's reduction: fp32 sums in rank order, rounded once (``reduce_grads(round_once=True)``,
@@ -30,14 +30,16 @@ def _gpus() -> int:
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-@pytest.mark.parametrize("push", ["kernel", "copyengine"])
+@pytest.mark.parametrize("push", ["kernel", "copyengine", "peer_cegather"])
 @pytest.mark.parametrize("world", [4, 8])
 def test_world_n_p2p_matches_round_once_oracle(world, push, tmp_path):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
     name = "bf16_world2"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", HYBRIDAGENT_B200_COMM="p2p", HYBRIDAGENT_B200_RECV_BYTES="16384",
-               HYBRIDAGENT_B200_PUSH_STREAMS="2" if push == "copyengine" else "0")
+               HYBRIDAGENT_B200_PUSH_STREAMS={"kernel": "0", "copyengine": "2", "peer_cegather": "peer"}[push])
+    if push == "peer_cegather":  # one copy-engine stream per peer; all-gather by the copy engines in parts
+        env.update(HYBRIDAGENT_B200_GATHER="ce", HYBRIDAGENT_B200_GATHER_PART_BYTES="4096")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={29800 + world}",
            os.path.join(HERE, "world_worker.py"), name, str(tmp_path)]
