@@ -11,6 +11,8 @@
 // depends only on the data and HA_SUMSQ_CHUNK, not on scheduling, and is far closer to
 // the exact sum than the reference's fp32 accumulation.  NaN and Inf propagate, so a
 // non-finite gradient anywhere makes the sum non-finite (the caller's skip decision).
+#include <cuda.h>
+
 #include <mutex>
 
 #include "ha_common.cuh"
@@ -174,7 +176,10 @@ extern "C" int ha_grad_sumsq(const ha_tensor* d_tensors, const ha_chunk* d_chunk
 //
 // The host-side name of a __device__ array is not a device address, so the address is
 // looked up with cudaGetSymbolAddress the first time the entry point runs on each device
-// (with that device current) and cached.  Every call shares the one array: two calls
+// (with that device current) and cached together with the unique ID of the CUDA context it
+// belongs to.  A later call on a different context of that device (the primary context was
+// reset with cudaDeviceReset and re-created) looks the address up again, so the cached
+// pointer never outlives its context.  Every call shares the one array: two calls
 // whose kernels overlap on the GPU (different streams, or different host threads) race on
 // it.  Each call writes every partial before reading it, so stale contents left by an
 // earlier call never reach a result and nothing needs clearing first.
@@ -184,20 +189,51 @@ namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mutex;
 double* g_noalloc_ptr[kMaxDevices] = {};
+unsigned long long g_noalloc_ctx[kMaxDevices] = {};
 
-// Device address of the partials array on the current device (looked up once per device).
+// Unique ID of the calling thread's current CUDA context (cuCtxGetCurrent + cuCtxGetId,
+// reached through the runtime's driver entry points), or 0 where the driver cannot say.
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(f);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr ||
+      get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// Device address of the partials array on the current device: looked up once per device
+// and context (cudaGetSymbolAddress with the device current), then reused.
 int noalloc_partials(double** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return ha::fail(HA_ERR_CUDA, "ha_grad_sumsq_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return ha::fail(HA_ERR_UNSUPPORTED, "ha_grad_sumsq_noalloc: device %d", dev);
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  const unsigned long long ctx = g_noalloc_ptr[dev] != nullptr ? current_context_id() : 0;
+  if (g_noalloc_ptr[dev] == nullptr || (ctx != 0 && ctx != g_noalloc_ctx[dev])) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, ha_noalloc_sumsq_partials);
     if (e != cudaSuccess || p == nullptr)
       return ha::fail(HA_ERR_CUDA, "ha_grad_sumsq_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
     g_noalloc_ptr[dev] = static_cast<double*>(p);
+    g_noalloc_ctx[dev] = current_context_id();  // the lookup made the device's context current
   }
   *out = g_noalloc_ptr[dev];
   return HA_OK;

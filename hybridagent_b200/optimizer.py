@@ -52,8 +52,8 @@ Deliberate differences (documented surface):
   not if one was modified in place (the reference's trainer does neither).
 * ``land_grads=True`` (new, opt-in, p2p mode) pushes the first two exchange rounds of each
   gradient to its owner while backward is still running (post-accumulate-grad hooks); results
-  are unchanged, but a gradient modified in place after its last landing and before
-  ``all_reduce_grads`` is not sent again (a replaced one is).
+  are unchanged: a gradient replaced, or modified in place through torch (its version counter
+  moves), after its last landing is sent again whole by ``all_reduce_grads``.
 * ``use_8bit=True`` (bitsandbytes PagedAdamW8bit, optimizer.py:76-86) is not provided.
 * ``state_dict`` / ``load_state_dict`` are new (the reference has neither).
 """
@@ -394,7 +394,7 @@ class ZeroOneAdamW:
         self.landing_enabled = False  # gradient landing active (toggle it off for non-final backward passes)
         self.land_launches = 0  # early pushes launched from the landing hooks
         self._land_hooks: list = []
-        self._landed: dict[int, torch.Tensor] = {}
+        self._landed: dict[int, tuple[torch.Tensor, int]] = {}  # index -> (gradient, its version when pushed)
         if land_grads and self.comm_mode == "p2p":
             self._setup_landing()
 
@@ -632,6 +632,19 @@ class ZeroOneAdamW:
 
         self._land_hooks = [p.register_post_accumulate_grad_hook(hook(i)) for i, p in enumerate(self.params)]
         self.landing_enabled = True
+        # peers' host-side heartbeats, checked before every early push (which runs before any
+        # deadline-bound collective): with a stale peer the push is left to all_reduce_grads
+        self._liveness = None
+        self.land_skipped = 0
+        try:
+            import torch.distributed as dist
+            store = dist.distributed_c10d._get_default_store() if dist.is_initialized() else None
+        except Exception:  # noqa: BLE001 -- no process-group store: no heartbeat
+            store = None
+        if store is not None:
+            from .liveness import Heartbeat
+            self._liveness = Heartbeat(store, self.rank, self.world,
+                                       deadline_s=float(os.environ.get("HYBRIDAGENT_B200_LAND_DEADLINE_S", "3.0")))
 
     def _on_landed(self, i: int, p: torch.Tensor) -> None:
         """Post-accumulate-grad hook of parameter i (runs on the autograd engine's thread)."""
@@ -647,7 +660,7 @@ class ZeroOneAdamW:
                 or not g.is_contiguous() or not len(c.land_pieces[k])):
             self._landed.pop(i, None)  # all_reduce_grads pushes it
             return
-        self._landed[i] = g
+        self._landed[i] = (g, g._version)
         self._land_pending.append((ci, k, g, torch.cuda.current_stream(self.device)))
         self._land_pending_bytes += g.numel() * g.element_size()
         if not self._land_callback:
@@ -664,6 +677,13 @@ class ZeroOneAdamW:
         """Pushes the pending landed gradients' early pieces on the landing stream."""
         pending, self._land_pending, self._land_pending_bytes = self._land_pending, [], 0
         if not pending:
+            return
+        if self._liveness is not None and not self._liveness.all_fresh():
+            # a peer's heartbeat is stale: push nothing into its memory now; the exchange sends
+            # these gradients after its collective has confirmed every rank (or raised CommFailure)
+            for ci, k, _, _ in pending:
+                self._landed.pop(self._classes[ci].layout.indices[k], None)
+            self.land_skipped += 1
             return
         land = self._land_stream
         with torch.cuda.device(self.device):
@@ -786,8 +806,10 @@ class ZeroOneAdamW:
                     done = None
                     if landed:  # pieces pushed while their gradient landed, gradient unchanged: skipped
                         done = np.zeros(len(c.layout.indices), dtype=bool)
-                        for i, g in landed.items():
-                            if self._entry_of[i][0] == ci and self.params[i].grad is g:
+                        for i, (g, version) in landed.items():
+                            # the same object, not modified in place since its push (in-place ops
+                            # such as p.grad.div_() bump the version counter)
+                            if self._entry_of[i][0] == ci and self.params[i].grad is g and g._version == version:
                                 done[self._entry_of[i][1]] = True
                     src = layout.piece_sources(c.pieces, ptrs, c.packed_param.element_size(), c.piece_dst, done)
                     c.move.np["src"][:len(src)] = src
@@ -1017,6 +1039,9 @@ class ZeroOneAdamW:
         for h in getattr(self, "_land_hooks", []):
             h.remove()
         self._land_hooks = []
+        if getattr(self, "_liveness", None) is not None:
+            self._liveness.stop()
+            self._liveness = None
         self.landing_enabled = False
         if getattr(self, "_peer_map", None) is not None:
             torch.cuda.synchronize(self.device)  # every stream of this rank, peer stores included

@@ -4,8 +4,10 @@ Each rank allocates its packed parameter buffer and its gradient receive buffer 
 library's ``ha_malloc`` (plain cudaMalloc, so CUDA IPC can share them), exposes them to
 torch as zero-copy tensors, hands the 64-byte IPC handles to every rank over the caller's
 process group, and maps every peer's buffers with ``ha_ipc_open``.  The mapped peer
-addresses are only ever used by this library's own kernels (plain loads / stores); no
-torch or library operation is given a peer address.
+addresses go only to this library's own kernels (plain loads / stores) and to the copy
+engines through ``cudaMemcpyAsync`` / ``cudaMemsetAsync`` in ``ha_copy_async`` (the gradient
+push, the parameter all-gather and the early pushes of gradient landing); no other library's
+kernel (torch, NCCL, cuBLAS) is ever given a peer address.
 """
 from __future__ import annotations
 

@@ -64,6 +64,9 @@ class Case:
     # "inf" / "nan": one element replaced
     overrides: dict = field(default_factory=dict)
     call_step_after_nonfinite: bool = True
+    # store per-tensor SHA-256 digests and seeded sample positions instead of whole arrays
+    # (full-size configurations whose arrays would not belong in the repository)
+    digest: bool = False
 
     @property
     def numels(self) -> list[int]:
@@ -138,4 +141,28 @@ CASES = [
          call_step_after_nonfinite=False),
 ]
 
-CASES_BY_NAME = {c.name: c for c in CASES}
+# BASELINE configuration 1 at its real shapes: 48 x (256, 512), 8 x (1024, 256), 8 x (65536,),
+# fp32, grads ~N(0, 1e-3) fresh every step, lr 1e-6, wd 0.01, clip 1.0, 10 steps (the global norm
+# is ~2.99, so every step clips)
+CONFIG1 = [(256, 512)] * 48 + [(1024, 256)] * 8 + [(65536,)] * 8
+DIGEST_CASES = [Case("cfg1_full", 13, CONFIG1, F32, steps=10, grad_sigma=1e-3, digest=True)]
+
+CASES_BY_NAME = {c.name: c for c in CASES + DIGEST_CASES}
+
+SAMPLES = 50_000
+
+
+def sample_positions(case: Case) -> tuple[np.ndarray, np.ndarray]:
+    """(tensor, offset) of the sampled elements of a digest case: SAMPLES seeded positions
+    over the whole parameter list plus every tensor's first and last element."""
+    bounds = np.concatenate([[0], np.cumsum(case.numels)]).astype(np.int64)
+    flat = np.random.default_rng([case.case_id, 99]).integers(0, int(bounds[-1]), size=SAMPLES)
+    flat = np.unique(np.concatenate([flat, bounds[:-1], bounds[1:] - 1]))
+    tensor = np.searchsorted(bounds, flat, side="right") - 1
+    return tensor.astype(np.int64), (flat - bounds[tensor]).astype(np.int64)
+
+
+def digest(a: np.ndarray) -> str:
+    """SHA-256 of an array's little-endian bytes (fp32 values, or 16-bit patterns)."""
+    import hashlib
+    return hashlib.sha256(np.ascontiguousarray(a).reshape(-1).tobytes()).hexdigest()

@@ -4,14 +4,16 @@
 
 Run in the build container, where the reference checkout exists:
 
-    python tests/golden/make_golden.py --reference <path to the HybridAgent checkout>
+    python tests/golden/make_golden.py --reference <path to the HybridAgent checkout> [--only <case>]
 
 The fixtures are committed; nothing on the GPU machines runs this script.
 
 Each step follows the caller order of hybrid_rl/train.py:248-295: zero_grad, set grads,
 all_reduce_grads, clip_grad_norm(max_norm), step.  Stored per case: the norm returned by
 every step, the final parameter of every tensor (dtype bit patterns), the owner's final
-master / exp_avg / exp_avg_sq / param_steps, and the owner map.
+master / exp_avg / exp_avg_sq / param_steps, and the owner map.  Full-size cases
+(``digest=True``: BASELINE configuration 1 at its real shapes) store instead the SHA-256 of
+every final array and the values at seeded sample positions (``cases.sample_positions``).
 """
 from __future__ import annotations
 
@@ -27,7 +29,7 @@ import torch.multiprocessing as mp
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
-from cases import BF16, CASES, F16, F32  # noqa: E402
+from cases import BF16, CASES, DIGEST_CASES, F16, F32, digest, sample_positions  # noqa: E402
 
 TORCH_DTYPE = {F32: torch.float32, BF16: torch.bfloat16, F16: torch.float16}
 
@@ -101,7 +103,7 @@ def main() -> None:
     ap.add_argument("--reference", required=True, help="HybridAgent checkout containing hybrid_rl/")
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
-    for k, case in enumerate(CASES):
+    for k, case in enumerate(CASES + DIGEST_CASES):
         if args.only and case.name != args.only:
             continue
         if case.world == 1:
@@ -126,6 +128,13 @@ def main() -> None:
                         assert np.array_equal(out[key], val), "ranks disagree on " + key
                     elif key == "norms":
                         assert np.array_equal(out[key], val, equal_nan=True), "ranks disagree on norms"
+        if case.digest:  # full-size case: digests of every final array and the sampled elements
+            full, out = out, {"norms": out["norms"], "owner": out["owner"]}
+            tensor, offset = sample_positions(case)
+            for key in ("param", "master", "exp_avg", "exp_avg_sq"):
+                out[f"sha256_{key}"] = np.array([digest(full[f"{key}_{i}"]) for i in range(len(case.shapes))])
+                out[f"sample_{key}"] = np.array([full[f"{key}_{t}"][o] for t, o in zip(tensor, offset)])
+            out["param_steps"] = np.array([int(full[f"param_steps_{i}"]) for i in range(len(case.shapes))])
         out["meta"] = np.array(json.dumps({"case": case.name, "torch": torch.__version__,
                                            "cpu_capability": torch.backends.cpu.get_cpu_capability()}))
         path = os.path.join(HERE, f"{case.name}.npz")

@@ -10,6 +10,6 @@ def test_landing_hook_forgets_a_push_when_the_gradient_changes_unpushed():
     from hybridagent_b200.optimizer import ZeroOneAdamW
     grad = object()
     for enabled, ok in ((False, True), (True, False)):
-        stub = SimpleNamespace(landing_enabled=enabled, _land_ok=ok, _landed={3: grad, 4: grad})
+        stub = SimpleNamespace(landing_enabled=enabled, _land_ok=ok, _landed={3: (grad, 0), 4: (grad, 0)})
         ZeroOneAdamW._on_landed(stub, 3, SimpleNamespace(grad=grad))
-        assert stub._landed == {4: grad}
+        assert stub._landed == {4: (grad, 0)}

