@@ -318,6 +318,7 @@ def checked_step(opt, params, inputs, numels, per_rank: int, max_norm: float = 1
     if world > 1:
         dist.all_reduce(acc)
     norm = opt.clip_grad_norm(max_norm)
+    p_pre = sp.take(lambda i: params[i].detach(), gdt)
     opt.step()
     sync()
     st_post = [sp.gather(sp.take(mine(d), torch.float32)) for d in (opt.master, opt.exp_avg, opt.exp_avg_sq)]
@@ -362,7 +363,8 @@ def checked_step(opt, params, inputs, numels, per_rank: int, max_norm: float = 1
         max_ulp = max(max_ulp, int(d.max()))
     fields["param_every_rank"] = int((p_post.view(bits) != p_exp.view(bits)[None]).sum())
     rel = abs(norm - exact) / exact if exact else abs(norm)
-    return {"checked_positions": sp.k, "checked_values": sp.k * (4 + world), "mismatches": sum(fields.values()),
+    changed = float((p_post[0].view(bits) != p_pre.view(bits)).double().mean())
+    return {"changed_param_fraction": changed, "checked_positions": sp.k, "checked_values": sp.k * (4 + world), "mismatches": sum(fields.values()),
             "max_ulp": max_ulp, "fields": fields,
             "norm": {"returned": norm, "fp64_of_reduced": exact, "rel_err": rel, "ok": bool(rel <= 1e-6)},
             "reduction": "exact (W<=2)" if world <= 2 else f"fp32 rank-order sum rounded once to {str(gdt)[6:]}",
@@ -673,39 +675,55 @@ def run_ours(args) -> None:
                 "(profiles/adamw_kernel_qwen3_8b.json), times this launch's parameters"}
     roofline, nvlink = hbm_roof, None
     if world > 1 and opt.comm_mode == "p2p":
-        # data crossing NVLink per step and GPU: the gradients this rank sends to their owners and
-        # the parameters it receives ((W-1)/W of 2 B/param each way); target time of a phase =
-        # max(its HBM bytes / HBM peak, its NVLink bytes / link peak)
+        # per phase: its HBM bytes and the bytes it moves over NVLink per GPU; the phase is bound by
+        # whichever takes longer at its measured peak, and the roofline line names the longest
+        # phase with that resource.  push: this rank's gradients of the other ranks' tensors
+        # ((W-1)/W of 2 B/param).  adamw: the update (28 B per owned param in HBM) and the
+        # parameter all-gather: 2 B x (W-1) per owned param with the copy engines, or -- the
+        # fused update -- only the 4-element groups whose bf16 value changed (the changed fraction
+        # is the checked step's, sampled; groups ~ 1-(1-p)^4 of them)
         link, link_src = measured_link_peak(world)
         foreign = n_params - owned_params
-        push_link = 2 * foreign
-        adamw_link = 2 * owned_params * (world - 1)
         push_how = ("copy engines, one stream per peer" if opt.push_streams < 0 else
                     f"copy engines on {opt.push_streams} streams + gather_kernel" if opt.push_streams > 0 else
                     "gather_kernel peer stores")
-        gather_how = ("adamw_kernel<bf16> in parts + copy-engine all-gather" if opt.gather_mode == "ce"
-                      else "adamw_kernel<bf16, PEERS> (peer stores fused)")
-        nvlink = {"link_peak_gbs": link, "link_peak_source": link_src, "nominal_gbs": NOMINAL_NVLINK_GBS}
-        for name, how, link_bytes, hbm_bytes in (("push", push_how, push_link, 4 * n_params),
-                                                 ("adamw", gather_how, adamw_link, algo + 2 * foreign)):
+        if opt.gather_mode == "ce":
+            gather_how, moved = "adamw_kernel<bf16> in parts + copy-engine all-gather", 1.0
+        else:
+            p = parity["changed_param_fraction"] if parity else 1.0
+            gather_how = "adamw_kernel<bf16, PEERS>: peer stores of the changed 4-element groups, fused"
+            moved = 1.0 - (1.0 - p) ** 4
+        adamw_link = int(2 * owned_params * (world - 1) * moved)
+        nvlink = {"link_peak_gbs": link, "link_peak_source": link_src, "nominal_gbs": NOMINAL_NVLINK_GBS,
+                  "all_gather_fraction_moved": round(moved, 6)}
+        # HBM: push -- read every gradient, write this rank's own pieces and receive the peers'
+        # (~2 B/param each way); adamw -- 28 B per owned param plus the peers' parameter stores landing here
+        for name, how, link_bytes, hbm_bytes in (("push", push_how, 2 * foreign, 4 * n_params),
+                                                 ("adamw", gather_how, adamw_link, algo + int(2 * foreign * moved))):
             ms_phase = phases.get(name)
             if not ms_phase:
                 continue
-            target = max(hbm_bytes / (peak * 1e9), link_bytes / (link * 1e9)) * 1e3
+            t_hbm, t_link = hbm_bytes / (peak * 1e9), link_bytes / (link * 1e9)
+            bound = "nvlink" if t_link >= t_hbm else "hbm"
             gbs = link_bytes / (ms_phase * 1e-3) / 1e9
-            nvlink[name] = {"how": how, "measured_ms": round(ms_phase, 3), "target_ms": round(target, 3),
-                            "frac": round(target / ms_phase, 4), "nvlink_bytes": link_bytes, "hbm_bytes": hbm_bytes,
-                            "link_gbs_achieved": round(gbs, 1), "frac_of_link_peak": round(gbs / link, 4),
-                            "frac_of_nominal": round(gbs / NOMINAL_NVLINK_GBS, 4)}
+            nvlink[name] = {"how": how, "bound": bound, "measured_ms": round(ms_phase, 3),
+                            "target_ms": round(max(t_hbm, t_link) * 1e3, 3),
+                            "frac": round(max(t_hbm, t_link) * 1e3 / ms_phase, 4), "nvlink_bytes": link_bytes,
+                            "hbm_bytes": hbm_bytes, "link_gbs_achieved": round(gbs, 1),
+                            "hbm_gbs_achieved": round(hbm_bytes / (ms_phase * 1e-3) / 1e9, 1),
+                            "frac_of_link_peak": round(gbs / link, 4),
+                            "frac_of_nominal_link": round(gbs / NOMINAL_NVLINK_GBS, 4)}
         dom = max((k for k in ("push", "adamw") if k in nvlink), key=lambda k: nvlink[k]["measured_ms"], default=None)
-        if dom is not None:
+        if dom is not None and nvlink[dom]["bound"] == "nvlink":
             d = nvlink[dom]
             roofline = {"bound": "nvlink", "kernel": d["how"], "phase": dom, "achieved": d["link_gbs_achieved"],
                         "peak": link, "unit": "GB/s", "frac": d["frac_of_link_peak"],
-                        "frac_of_nominal": d["frac_of_nominal"], "peak_source": link_src,
+                        "frac_of_nominal": d["frac_of_nominal_link"], "peak_source": link_src,
                         "algorithmic_bytes_per_launch": d["nvlink_bytes"], "traffic": None,
                         "traffic_source": "NVLink bytes are algorithmic; ncu's NVLink counters were not readable "
                                           "on this pool", "hbm_adamw": hbm_roof}
+        elif dom is not None:
+            roofline = dict(hbm_roof, phase=dom)
     out = {
         "metric": "ZeRO-1 AdamW step Gparams/s",
         "value": round(n_params / (ms_max * 1e-3) / 1e9, 3),

@@ -55,41 +55,56 @@ struct Peers {
   int64_t delta[HA_MAX_PEERS];
 };
 
-// The new parameter value of 4 elements at local address `local` also goes to every peer.
-template <int DT, bool PEERS>
-__device__ __forceinline__ void push4(const Peers& p, uint64_t local, int64_t e, float4 x) {
-  if constexpr (PEERS) {
+// Four values rounded to a 16-bit DT, packed as one 8-byte word.
+template <int DT>
+__device__ __forceinline__ uint2 pack4(float4 x) {
+  return make_uint2(uint32_t(Elem<DT>::narrow(x.x)) | (uint32_t(Elem<DT>::narrow(x.y)) << 16),
+                    uint32_t(Elem<DT>::narrow(x.z)) | (uint32_t(Elem<DT>::narrow(x.w)) << 16));
+}
+
+// The same 8 bytes at `local` + e in every peer's copy of the packed parameter buffer.
+__device__ __forceinline__ void push_raw4(const Peers& p, uint64_t local, int64_t e, uint2 w) {
 #pragma unroll
-    for (int q = 0; q < HA_MAX_PEERS; ++q) {  // constant indices keep delta[] in the parameter bank
-      if (q >= p.n) break;
-      void* dst = reinterpret_cast<void*>(local + p.delta[q]);
-      if constexpr (DT == HA_F32) {
-        store4_f32(static_cast<float*>(dst), e, x);
-      } else {
-        store4_narrow<DT>(dst, e, x);
-      }
-    }
+  for (int q = 0; q < HA_MAX_PEERS; ++q) {  // constant indices keep delta[] in the parameter bank
+    if (q >= p.n) break;
+    __stcs(reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(local + p.delta[q]) + e), w);
   }
 }
 
-template <int DT, bool PEERS>
-__device__ __forceinline__ void push1(const Peers& p, uint64_t local, int64_t k, float x) {
-  if constexpr (PEERS) {
+__device__ __forceinline__ void push_f32x4(const Peers& p, uint64_t local, int64_t e, float4 x) {
 #pragma unroll
-    for (int q = 0; q < HA_MAX_PEERS; ++q) {
-      if (q >= p.n) break;
-      if constexpr (DT == HA_F32) {
-        reinterpret_cast<float*>(local + p.delta[q])[k] = x;
-      } else {
-        reinterpret_cast<uint16_t*>(local + p.delta[q])[k] = Elem<DT>::narrow(x);
-      }
+  for (int q = 0; q < HA_MAX_PEERS; ++q) {
+    if (q >= p.n) break;
+    store4_f32(reinterpret_cast<float*>(local + p.delta[q]), e, x);
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void push1(const Peers& p, uint64_t local, int64_t k, float x) {
+#pragma unroll
+  for (int q = 0; q < HA_MAX_PEERS; ++q) {
+    if (q >= p.n) break;
+    if constexpr (DT == HA_F32) {
+      reinterpret_cast<float*>(local + p.delta[q])[k] = x;
+    } else {
+      reinterpret_cast<uint16_t*>(local + p.delta[q])[k] = Elem<DT>::narrow(x);
     }
   }
 }
 
 // DT is the gradient and parameter dtype.  For HA_F32 the master is the parameter
-// (optimizer.py:71-73) and no separate copy is written.  PEERS: the new parameter values
-// are also stored into every peer's copy of the packed parameter buffer.
+// (optimizer.py:71-73) and no separate copy is written.  PEERS: the parameter all-gather is
+// fused in -- every new parameter value also goes to the same place in every peer's copy of
+// the packed parameter buffer (the per-tensor dist.broadcast of optimizer.py:192-194).
+//
+// With PEERS and a 16-bit parameter only the 4-element groups whose rounded value changed are
+// stored, locally and to the peers: the kernel reads the parameter's current bits (which every
+// rank holds identically -- the previous update stored them everywhere) and compares them with
+// the new ones.  Every copy ends with exactly the bits a full broadcast would leave, but with the
+// small learning rates of RL fine-tuning most bf16 parameters do not move in a step, so the
+// NVLink traffic of the all-gather shrinks with the fraction that does: reading the old
+// parameter (2 B) replaces writing it (2 B) in HBM, and the 2 B x (W-1) of peer stores are paid
+// only for changed groups.
 template <int DT, bool PEERS>
 __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __restrict__ tensors,
                                                          const ha_chunk* __restrict__ chunks, Scalars s, Peers peers) {
@@ -106,6 +121,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
   void* param = reinterpret_cast<void*>(t.param);
   const float decay = t.decay, neg_lr = t.neg_lr, rc1 = t.rc1, rc2 = t.rc2;
   const uint64_t pushed = DT == HA_F32 ? t.master : t.param;  // the parameter's local address
+  constexpr bool kDelta = PEERS && DT != HA_F32;                // stores of changed groups only
 
   constexpr uint64_t kNarrowAlign = DT == HA_F32 ? 15 : 7;
   const bool vec = ((t.master | t.exp_avg | t.exp_avg_sq) & 15) == 0 && (t.grad & kNarrowAlign) == 0 &&
@@ -113,6 +129,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
   if (vec) {
     for (int64_t base = begin; base < end; base += kPass) {
       float4 g[kGroups], ms[kGroups], m[kGroups], v[kGroups];
+      uint2 old[kGroups];
       int64_t e[kGroups];
 #pragma unroll
       for (int u = 0; u < kGroups; ++u) {
@@ -122,6 +139,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
           ms[u] = load4_f32(master, e[u]);
           m[u] = load4_f32(exp_avg, e[u]);
           v[u] = load4_f32(exp_avg_sq, e[u]);
+          if constexpr (kDelta) old[u] = __ldcs(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(param) + e[u]));
         }
       }
 #pragma unroll
@@ -134,8 +152,15 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
           store4_f32(master, e[u], ms[u]);
           store4_f32(exp_avg, e[u], m[u]);
           store4_f32(exp_avg_sq, e[u], v[u]);
-          if constexpr (DT != HA_F32) store4_narrow<DT>(param, e[u], ms[u]);
-          push4<DT, PEERS>(peers, pushed, e[u], ms[u]);
+          if constexpr (DT != HA_F32) {
+            const uint2 w = pack4<DT>(ms[u]);
+            if (!kDelta || w.x != old[u].x || w.y != old[u].y) {
+              __stcs(reinterpret_cast<uint2*>(static_cast<uint16_t*>(param) + e[u]), w);
+              if constexpr (PEERS) push_raw4(peers, pushed, e[u], w);
+            }
+          } else if constexpr (PEERS) {
+            push_f32x4(peers, pushed, e[u], ms[u]);
+          }
         } else {
           for (int64_t k = e[u]; k < end; ++k) {  // ragged tail of the tensor (one thread)
             float a = master[k], b = exp_avg[k], c = exp_avg_sq[k];
@@ -143,8 +168,15 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
             master[k] = a;
             exp_avg[k] = b;
             exp_avg_sq[k] = c;
-            if constexpr (DT != HA_F32) static_cast<uint16_t*>(param)[k] = Elem<DT>::narrow(a);
-            push1<DT, PEERS>(peers, pushed, k, a);
+            if constexpr (DT != HA_F32) {
+              const uint16_t w = Elem<DT>::narrow(a);
+              if (!kDelta || w != static_cast<const uint16_t*>(param)[k]) {
+                static_cast<uint16_t*>(param)[k] = w;
+                if constexpr (PEERS) push1<DT>(peers, pushed, k, a);
+              }
+            } else if constexpr (PEERS) {
+              push1<DT>(peers, pushed, k, a);
+            }
           }
         }
       }
@@ -156,8 +188,15 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
       master[k] = a;
       exp_avg[k] = b;
       exp_avg_sq[k] = c;
-      if constexpr (DT != HA_F32) static_cast<uint16_t*>(param)[k] = Elem<DT>::narrow(a);
-      push1<DT, PEERS>(peers, pushed, k, a);
+      if constexpr (DT != HA_F32) {
+        const uint16_t w = Elem<DT>::narrow(a);
+        if (!kDelta || w != static_cast<const uint16_t*>(param)[k]) {
+          static_cast<uint16_t*>(param)[k] = w;
+          if constexpr (PEERS) push1<DT>(peers, pushed, k, a);
+        }
+      } else if constexpr (PEERS) {
+        push1<DT>(peers, pushed, k, a);
+      }
     }
   }
 }

@@ -239,3 +239,77 @@ def test_gather(elem, how):
         want = torch.zeros_like(got) if k == 3 else srcs[k]
         assert torch.equal(got.view(torch.int16 if elem == 2 else torch.int32),
                            want.view(torch.int16 if elem == 2 else torch.int32)), k
+
+
+@pytest.mark.parametrize("code", [BF16, F16], ids=["bf16", "f16"])
+def test_adamw_peers_store_changed_groups_only(code):
+    """ha_adamw_step_peers with two 'peers' emulated on this GPU (arenas at fixed offsets from
+    the local parameter arena).  Local parameters and every peer end with the oracle's new
+    values wherever a 4-element group (per element on the scalar path and ragged tails)
+    changed; unchanged groups are not stored at all -- a sentinel planted in a peer's copy of an
+    unchanged group survives, one in a changed group is overwritten."""
+    import torch
+    sizes = SIZES + [3 * 16384 + 6]
+    n = len(sizes)
+    rng = np.random.default_rng(40 + code)
+    # half the tensors with a large learning rate (most rounded values move), half tiny (few do)
+    lrs = [1e-3 if k % 2 == 0 else 1e-9 for k in range(n)]
+    ts = Tensors(code, sizes, seed=30 + code, misalign=(4, 13), no_grad=(2, 17), lr=lrs)
+    offs, o = [], 0
+    for k, size in enumerate(sizes):
+        o += 1 if k in (4, 13) else 0  # the misaligned tensors keep an odd start in the arena
+        offs.append(o)
+        o = (o + size + 63) // 64 * 64
+    dt = ts.param[0].dtype
+    local = torch.zeros(o, dtype=dt, device="cuda")
+    for k, size in enumerate(sizes):
+        local[offs[k]:offs[k] + size].copy_(ts.param[k])
+        ts.tab[k]["param"] = local.data_ptr() + 2 * offs[k]
+    init = to_numpy(local, code)
+    peers = [torch.zeros(o, dtype=dt, device="cuda") for _ in range(2)]
+    planted = rng.choice(o, size=4000, replace=False)
+    peer_init = []
+    for p in peers:
+        bits = init.copy()
+        bits[planted] ^= 1  # sentinels: a peer copy that differs from the local one
+        p.copy_(to_torch(bits, code, device="cuda"))
+        peer_init.append(bits)
+    pe = _lib.Peers()
+    pe.n = 2
+    for q, p in enumerate(peers):
+        pe.delta[q] = p.data_ptr() - local.data_ptr()
+    table = ts.device_table(0.01)
+    chunks = layout.chunk_table(sizes, _lib.HA_ADAMW_CHUNK)
+    dchunks = _dev_bytes(chunks)
+    sc = _lib.AdamwScalars()
+    _lib.call("ha_make_scalars", B1, B2, EPS, 0.01, code, 0, 0.0, ctypes.byref(sc))
+    _lib.call("ha_adamw_step_peers", table.data_ptr(), dchunks.data_ptr(), len(chunks), _lib.HA_ADAMW_CHUNK, code, code,
+              ctypes.byref(sc), ctypes.byref(pe), _stream())
+    torch.cuda.synchronize()
+    got_local = to_numpy(local, code)
+    got_peers = [to_numpy(p, code) for p in peers]
+    changed_any = 0
+    for k, size in enumerate(sizes):
+        master, m, v = ts.np_master[k].copy(), ts.np_m[k].copy(), ts.np_v[k].copy()
+        param = ts.np_param[k].copy()
+        if ts.np_grad[k] is not None:
+            Z.adamw_tensor(Z.FORM_TORCH_CUDA, ts.np_grad[k], code, master, m, v, param, code, lr=float(ts.lrs[k]),
+                           beta1=B1, beta2=B2, eps=EPS, weight_decay=0.01, step=int(ts.steps[k]), clip_scale=None)
+        sl = slice(offs[k], offs[k] + size)
+        old = init[sl]
+        assert_bits_equal(got_local[sl], param, f"local param[{k}]")
+        # which elements were stored: the element's 4-group changed (vector path: whole groups of
+        # an aligned tensor), or the element itself (scalar path, ragged tail)
+        diff = param != old
+        stored = diff.copy()
+        if ts.np_grad[k] is not None and k not in (4, 13):
+            full = size // 4 * 4
+            grp = diff[:full].reshape(-1, 4).any(axis=1)
+            stored[:full] = np.repeat(grp, 4)
+        changed_any += int(diff.sum())
+        for q in range(2):
+            want = np.where(stored, param, peer_init[q][sl])
+            assert_bits_equal(got_peers[q][sl], want, f"peer {q} param[{k}]")
+    assert changed_any > 1000  # the large-lr tensors moved
+    survived = int((got_peers[0][planted] == peer_init[0][planted]).sum())
+    assert survived > 1000  # most sentinels sat in unchanged groups of the tiny-lr tensors
