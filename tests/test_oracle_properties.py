@@ -47,7 +47,9 @@ def test_oracle_cpu_form_matches_torch_cpu(dtype, n, lr, wd, step, beta1, beta2,
                   master_is_parameter=param is None)
     assert_bits_equal(oea, tm.numpy(), "exp_avg")
     assert_bits_equal(oeas, tv.numpy(), "exp_avg_sq")
-    assert_state_close(om, tmaster.numpy(), "master")
+    # the oracle's correctly rounded sqrt vs MKL's on this host: the update term may move by an
+    # ulp of lr (the documented master exception), visible only where the master is near zero
+    assert_state_close(om, tmaster.numpy(), "master", lr_ulps=(lr, 2))
     if param is not None:
         assert_bits_equal(op, Z.narrow(om, dtype, Z.FORM_TORCH_CPU), "param = RNE(master)")
         assert_bits_equal(to_numpy(tparam, dtype), Z.narrow(tmaster.numpy(), dtype, Z.FORM_TORCH_CPU),
