@@ -97,17 +97,18 @@ __device__ __forceinline__ void push1(const Peers& p, uint64_t local, int64_t k,
 // fused in -- every new parameter value also goes to the same place in every peer's copy of
 // the packed parameter buffer (the per-tensor dist.broadcast of optimizer.py:192-194).
 //
-// With PEERS and a 16-bit parameter only the 4-element groups whose rounded value changed are
-// stored, locally and to the peers: the kernel reads the parameter's current bits (which every
-// rank holds identically -- the previous update stored them everywhere) and compares them with
-// the new ones.  Every copy ends with exactly the bits a full broadcast would leave, but with the
-// small learning rates of RL fine-tuning most bf16 parameters do not move in a step, so the
-// NVLink traffic of the all-gather shrinks with the fraction that does: reading the old
-// parameter (2 B) replaces writing it (2 B) in HBM, and the 2 B x (W-1) of peer stores are paid
-// only for changed groups.
-template <int DT, bool PEERS>
+// DELTA (16-bit parameters): a 4-element group of the parameter copy is stored -- locally and,
+// with PEERS, to every peer -- only if its rounded value changed, i.e. if RNE(new master)
+// differs from RNE(old master).  The caller guarantees that every copy of the parameter holds
+// RNE(old master) on entry (the optimizer falls back to the dense kernel for a step after
+// anything else wrote a parameter or a master); every copy then ends with exactly the bits a
+// full write would leave.  With the small learning rates of RL fine-tuning few bf16 values move
+// in a step, so this saves the 2 B/param parameter write in HBM and nearly all of the
+// all-gather's NVLink bytes.
+template <int DT, bool PEERS, bool DELTA>
 __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __restrict__ tensors,
                                                          const ha_chunk* __restrict__ chunks, Scalars s, Peers peers) {
+  static_assert(!(DELTA && DT == HA_F32), "fp32 parameters are their own masters: always written");
   __shared__ StagedChunk sc;
   stage_chunk(tensors, chunks, &sc);
   const ha_tensor& t = sc.t;
@@ -121,15 +122,31 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
   void* param = reinterpret_cast<void*>(t.param);
   const float decay = t.decay, neg_lr = t.neg_lr, rc1 = t.rc1, rc2 = t.rc2;
   const uint64_t pushed = DT == HA_F32 ? t.master : t.param;  // the parameter's local address
-  constexpr bool kDelta = PEERS && DT != HA_F32;                // stores of changed groups only
 
   constexpr uint64_t kNarrowAlign = DT == HA_F32 ? 15 : 7;
   const bool vec = ((t.master | t.exp_avg | t.exp_avg_sq) & 15) == 0 && (t.grad & kNarrowAlign) == 0 &&
                    (DT == HA_F32 || (t.param & kNarrowAlign) == 0);
+  // one element on the scalar paths (ragged tails, unaligned tensors)
+  auto one = [&](int64_t k) {
+    float a = master[k], b = exp_avg[k], c = exp_avg_sq[k];
+    const float before = a;
+    adamw_elem(s, decay, neg_lr, rc1, rc2, grad_in<DT>(s, load1<DT>(grad, k)), a, b, c);
+    master[k] = a;
+    exp_avg[k] = b;
+    exp_avg_sq[k] = c;
+    if constexpr (DT != HA_F32) {
+      const uint16_t w = Elem<DT>::narrow(a);
+      if (!DELTA || w != Elem<DT>::narrow(before)) {
+        static_cast<uint16_t*>(param)[k] = w;
+        if constexpr (PEERS) push1<DT>(peers, pushed, k, a);
+      }
+    } else if constexpr (PEERS) {
+      push1<DT>(peers, pushed, k, a);
+    }
+  };
   if (vec) {
     for (int64_t base = begin; base < end; base += kPass) {
       float4 g[kGroups], ms[kGroups], m[kGroups], v[kGroups];
-      uint2 old[kGroups];
       int64_t e[kGroups];
 #pragma unroll
       for (int u = 0; u < kGroups; ++u) {
@@ -139,12 +156,13 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
           ms[u] = load4_f32(master, e[u]);
           m[u] = load4_f32(exp_avg, e[u]);
           v[u] = load4_f32(exp_avg_sq, e[u]);
-          if constexpr (kDelta) old[u] = __ldcs(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(param) + e[u]));
         }
       }
 #pragma unroll
       for (int u = 0; u < kGroups; ++u) {
         if (e[u] + 4 <= end) {
+          uint2 before = make_uint2(0, 0);
+          if constexpr (DELTA) before = pack4<DT>(ms[u]);
           adamw_elem(s, decay, neg_lr, rc1, rc2, grad_in<DT>(s, g[u].x), ms[u].x, m[u].x, v[u].x);
           adamw_elem(s, decay, neg_lr, rc1, rc2, grad_in<DT>(s, g[u].y), ms[u].y, m[u].y, v[u].y);
           adamw_elem(s, decay, neg_lr, rc1, rc2, grad_in<DT>(s, g[u].z), ms[u].z, m[u].z, v[u].z);
@@ -154,7 +172,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
           store4_f32(exp_avg_sq, e[u], v[u]);
           if constexpr (DT != HA_F32) {
             const uint2 w = pack4<DT>(ms[u]);
-            if (!kDelta || w.x != old[u].x || w.y != old[u].y) {
+            if (!DELTA || w.x != before.x || w.y != before.y) {
               __stcs(reinterpret_cast<uint2*>(static_cast<uint16_t*>(param) + e[u]), w);
               if constexpr (PEERS) push_raw4(peers, pushed, e[u], w);
             }
@@ -162,42 +180,12 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
             push_f32x4(peers, pushed, e[u], ms[u]);
           }
         } else {
-          for (int64_t k = e[u]; k < end; ++k) {  // ragged tail of the tensor (one thread)
-            float a = master[k], b = exp_avg[k], c = exp_avg_sq[k];
-            adamw_elem(s, decay, neg_lr, rc1, rc2, grad_in<DT>(s, load1<DT>(grad, k)), a, b, c);
-            master[k] = a;
-            exp_avg[k] = b;
-            exp_avg_sq[k] = c;
-            if constexpr (DT != HA_F32) {
-              const uint16_t w = Elem<DT>::narrow(a);
-              if (!kDelta || w != static_cast<const uint16_t*>(param)[k]) {
-                static_cast<uint16_t*>(param)[k] = w;
-                if constexpr (PEERS) push1<DT>(peers, pushed, k, a);
-              }
-            } else if constexpr (PEERS) {
-              push1<DT>(peers, pushed, k, a);
-            }
-          }
+          for (int64_t k = e[u]; k < end; ++k) one(k);  // ragged tail of the tensor (one thread)
         }
       }
     }
   } else {
-    for (int64_t k = begin + threadIdx.x; k < end; k += kThreads) {
-      float a = master[k], b = exp_avg[k], c = exp_avg_sq[k];
-      adamw_elem(s, decay, neg_lr, rc1, rc2, grad_in<DT>(s, load1<DT>(grad, k)), a, b, c);
-      master[k] = a;
-      exp_avg[k] = b;
-      exp_avg_sq[k] = c;
-      if constexpr (DT != HA_F32) {
-        const uint16_t w = Elem<DT>::narrow(a);
-        if (!kDelta || w != static_cast<const uint16_t*>(param)[k]) {
-          static_cast<uint16_t*>(param)[k] = w;
-          if constexpr (PEERS) push1<DT>(peers, pushed, k, a);
-        }
-      } else if constexpr (PEERS) {
-        push1<DT>(peers, pushed, k, a);
-      }
-    }
+    for (int64_t k = begin + threadIdx.x; k < end; k += kThreads) one(k);
   }
 }
 
@@ -243,9 +231,9 @@ extern "C" int ha_adamw_step(const ha_tensor* d_tensors, const ha_chunk* d_chunk
   const dim3 grid(static_cast<unsigned>(n_chunks));
   const Peers none{};
   switch (grad_dtype) {
-    case HA_F32: adamw_kernel<HA_F32, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none); break;
-    case HA_BF16: adamw_kernel<HA_BF16, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none); break;
-    default: adamw_kernel<HA_F16, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none); break;
+    case HA_F32: adamw_kernel<HA_F32, false, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none); break;
+    case HA_BF16: adamw_kernel<HA_BF16, false, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none); break;
+    default: adamw_kernel<HA_F16, false, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none); break;
   }
   return check_launch("adamw_kernel");
 }
@@ -275,11 +263,50 @@ extern "C" int ha_adamw_step_peers(const ha_tensor* d_tensors, const ha_chunk* d
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid(static_cast<unsigned>(n_chunks));
   switch (grad_dtype) {
-    case HA_F32: adamw_kernel<HA_F32, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p); break;
-    case HA_BF16: adamw_kernel<HA_BF16, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p); break;
-    default: adamw_kernel<HA_F16, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p); break;
+    case HA_F32: adamw_kernel<HA_F32, true, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p); break;
+    case HA_BF16: adamw_kernel<HA_BF16, true, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p); break;
+    default: adamw_kernel<HA_F16, true, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p); break;
   }
   return check_launch("adamw_kernel (peers)");
+}
+
+extern "C" int ha_adamw_step_delta(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,
+                                   int64_t chunk_elems, int param_dtype, const ha_adamw_scalars* sc,
+                                   const ha_peers* peers, void* stream) {
+  HA_NVTX_RANGE();
+  using namespace ha;
+  if (chunk_elems != HA_ADAMW_CHUNK)
+    return fail(HA_ERR_INVALID, "ha_adamw_step_delta: chunk_elems must be %d", HA_ADAMW_CHUNK);
+  if (param_dtype != HA_BF16 && param_dtype != HA_F16)
+    return fail(HA_ERR_UNSUPPORTED, "ha_adamw_step_delta: param dtype %d (16-bit parameters only)", param_dtype);
+  if (n_chunks < 0 || n_chunks > 0x7fffffffLL)
+    return fail(HA_ERR_INVALID, "ha_adamw_step_delta: n_chunks %lld", (long long)n_chunks);
+  if (sc == nullptr) return fail(HA_ERR_INVALID, "ha_adamw_step_delta: NULL scalars");
+  if (peers != nullptr) {
+    if (peers->n < 0 || peers->n > HA_MAX_PEERS) return fail(HA_ERR_INVALID, "ha_adamw_step_delta: %d peers", peers->n);
+    for (int q = 0; q < peers->n; ++q)
+      if ((peers->delta[q] & 15) != 0)
+        return fail(HA_ERR_INVALID, "ha_adamw_step_delta: peer %d offset not 16-byte aligned", q);
+  }
+  if (n_chunks == 0) return HA_OK;
+  if (d_tensors == nullptr || d_chunks == nullptr) return fail(HA_ERR_INVALID, "ha_adamw_step_delta: NULL table");
+  const Scalars s{sc->b1, sc->a1, sc->b2, sc->a2, sc->eps, sc->use_decay, sc->clip, sc->clip_mult};
+  Peers p{};
+  if (peers != nullptr) {
+    p.n = peers->n;
+    for (int q = 0; q < peers->n; ++q) p.delta[q] = peers->delta[q];
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid(static_cast<unsigned>(n_chunks));
+  const bool with_peers = peers != nullptr && p.n > 0;
+  if (param_dtype == HA_BF16) {
+    if (with_peers) adamw_kernel<HA_BF16, true, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p);
+    else adamw_kernel<HA_BF16, false, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p);
+  } else {
+    if (with_peers) adamw_kernel<HA_F16, true, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p);
+    else adamw_kernel<HA_F16, false, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p);
+  }
+  return check_launch("adamw_kernel (delta)");
 }
 
 extern "C" int ha_scale_grads(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,

@@ -375,17 +375,30 @@ class ZeroOneAdamW:
                 self._comm = NcclComm(self.rank, self.world, timeout_s=comm_timeout_s)
             self._classes = [_Class(self, c) for c in self._plan.classes]
             self._norm_buf = torch.zeros(len(self._classes), dtype=torch.float64, device=self.device)
-            self._used_dev = torch.zeros(len(self.params), dtype=torch.uint8, device=self.device)
+            # world > 1: one all-reduce(max) of [used(T), dirty(T)] (see _detect_dirty)
+            self._used_dev = torch.zeros(2 * len(self.params), dtype=torch.uint8, device=self.device)
             self._barrier_buf = torch.zeros(1, dtype=torch.int32, device=self.device)
             # pinned landing buffers of the host reads (deadline-aware waits at world > 1)
             self._norm_host = torch.zeros(len(self._classes), dtype=torch.float64, pin_memory=True)
             if self.world > 1:
                 # this rank's mask (uploaded asynchronously: the next call rewrites it only after
                 # reading the all-reduce that follows the upload) and the all-reduced mask
-                self._used_local = torch.zeros(len(self.params), dtype=torch.uint8, pin_memory=True)
-                self._used_host = torch.zeros(len(self.params), dtype=torch.uint8, pin_memory=True)
+                self._used_local = torch.zeros(2 * len(self.params), dtype=torch.uint8, pin_memory=True)
+                self._used_host = torch.zeros(2 * len(self.params), dtype=torch.uint8, pin_memory=True)
                 self._setup_world()
             torch.cuda.current_stream().synchronize()
+        # changed-groups-only parameter writes (ha_adamw_step_delta) need every copy of a parameter
+        # to hold RNE(master) on entry.  Torch's version counters tell when anything else wrote a
+        # parameter or a master; such tensors are "dirty" (the same set on every rank) and the
+        # next step writes every parameter in full, as the reference does.
+        self.delta_writes = os.environ.get("HYBRIDAGENT_B200_DELTA", "1") != "0"
+        self._dirty = np.zeros(len(self.params), dtype=bool)
+        self._force_dirty = np.zeros(len(self.params), dtype=bool)
+        self._seen_params = self._param_versions()
+        self._seen_masters = self._master_versions()
+        self._dense_this_step = True
+        self._last_used: np.ndarray | None = None  # world > 1: the used set of the last all_reduce_grads
+        self.dense_steps = 0  # steps that wrote every parameter (delta off, fp32 classes aside)
         self._pending_clip: float | None = None
         self._fused_sumsq: list | None = None
         self._grad_cache: dict[int, tuple] = {}
@@ -522,6 +535,46 @@ class ZeroOneAdamW:
         """Stream-ordered barrier across ranks: returns on every rank's stream only after every
         rank's earlier work (this rank's peer stores included) has completed."""
         self._comm.all_reduce_sum(self._barrier_buf, HA_I32)
+
+    # ---------------------------------------------------------------- dirty tracking
+    def _param_versions(self) -> np.ndarray:
+        """(address, torch version) of every parameter: a re-bound or in-place-modified
+        parameter shows up as a change."""
+        out = np.zeros((len(self.params), 2), dtype=np.int64)
+        for i, p in enumerate(self.params):
+            out[i, 0] = p.data_ptr()
+            out[i, 1] = p._version
+        return out
+
+    def _master_versions(self) -> list[int]:
+        """Torch version of each class's packed master buffer (the masters are views of it, so
+        an in-place write to any of them moves it); -1 for fp32 classes (master = parameter)."""
+        return [-1 if c.master_buf is None else c.master_buf._version for c in self._classes]
+
+    def _detect_dirty(self) -> np.ndarray:
+        """Tensors whose parameter (any rank's copy) or master was written by anything other than
+        this optimizer's kernels since the versions were last recorded, plus those marked with
+        mark_parameters_dirty(); records the current versions."""
+        now = self._param_versions()
+        dirty = (now != self._seen_params).any(axis=1) | self._force_dirty
+        masters = self._master_versions()
+        for c, was, is_ in zip(self._classes, self._seen_masters, masters):
+            if was != is_:
+                dirty[c.owned] = True
+        self._seen_params, self._seen_masters = now, masters
+        self._force_dirty[:] = False
+        return dirty
+
+    def mark_parameters_dirty(self, indices=None) -> None:
+        """Declares parameters (all, or the given flat indices) as written outside torch's
+        in-place ops -- through ``.data`` or a raw pointer -- so the next step writes them in
+        full on every rank, as the reference's broadcast would.  In-place torch writes
+        (``p.copy_``, a model's ``load_state_dict``, ``optimizer.master[i].copy_``) are detected
+        without it.  At world size > 1 call it before ``all_reduce_grads``."""
+        if indices is None:
+            self._force_dirty[:] = True
+        else:
+            self._force_dirty[np.asarray(list(indices), dtype=np.int64)] = True
 
     # ---------------------------------------------------------------- helpers
     def _phase(self, name: str, start: bool) -> None:
@@ -790,11 +843,16 @@ class ZeroOneAdamW:
                     keep.append(g)
                     ptrs[k] = g.data_ptr()
                 class_ptrs.append(ptrs)
+            T = len(self.params)
+            local[T:] = self._detect_dirty()  # every rank learns every rank's dirty tensors
             self._used_dev.copy_(self._used_local, non_blocking=True)  # no host wait: a peer may be missing
             self._comm.all_reduce_max(self._used_dev, HA_U8)
             # a rank that stopped answering ends here (CommFailure), before any peer store
-            used = self._comm.read(self._used_dev, self._used_host, "all-reduce(max) of the used mask")
-            used = used.numpy().astype(bool)
+            both = self._comm.read(self._used_dev, self._used_host, "all-reduce(max) of the used mask")
+            both = both.numpy().astype(bool)
+            used = both[:T]
+            self._dirty |= both[T:]
+            self._last_used = used
             if self._land_hooks:  # the early pushes have all completed: rewind their arena
                 self._land_cursor = [0, 0]
                 self._land_waited = False
@@ -924,21 +982,39 @@ class ZeroOneAdamW:
         scale, self._pending_clip = self._pending_clip, None
         with torch.cuda.device(self.device):
             launches, keep = [], []
+            updated = np.zeros(len(self.params), dtype=bool)  # tensors this step writes (the used set)
             for k, c in enumerate(self._classes):
                 grads, ptrs = self._cached_grads(k, c)
                 keep.append(grads)
                 self._upload_table(c, ptrs, advance=True)
+                updated[np.asarray(c.owned, dtype=np.int64)[ptrs != 0]] = True
                 sc = _lib.AdamwScalars()
                 _lib.call("ha_make_scalars", self.betas[0], self.betas[1], self.eps, self.weight_decay, c.code,
                           0 if scale is None else 1, 0.0 if scale is None else scale, ctypes.byref(sc))
                 launches.append((c, sc))
+            if self.world == 1:
+                self._dirty |= self._detect_dirty()
+            elif self._last_used is not None:
+                updated = self._last_used  # every rank's owners update exactly the used tensors
+            else:  # no all_reduce_grads before this step: clear nothing (the set must stay collective)
+                updated = np.zeros(len(self.params), dtype=bool)
+            self._last_used = None
             p2p = self.comm_mode == "p2p"
+            # changed-groups-only writes (16-bit classes) unless some parameter or master was written
+            # behind the optimizer's back: then this step writes everything, as the reference does
+            dense = not self.delta_writes or bool(self._dirty.any())
+            self._dense_this_step = dense
+            self.dense_steps += dense
             self._phase("adamw", True)
             ce_gather = p2p and self.gather_mode == "ce"
             main = torch.cuda.current_stream()
             for c, sc in launches:
                 chunks, n = c.adamw_chunks
-                if n and ce_gather:  # update in parts; the copy engines send each finished part to the peers
+                if n and not dense and c.code != HA_F32 and not ce_gather and self.comm_mode != "nccl":
+                    _lib.call("ha_adamw_step_delta", c.table.ptr, chunks.data_ptr(), n, HA_ADAMW_CHUNK, c.code,
+                              ctypes.byref(sc), ctypes.byref(c.peers) if p2p else None, self._stream())
+                    self.launches += 1
+                elif n and ce_gather:  # update in parts; the copy engines send each finished part to the peers
                     esz = c.packed_param.element_size()
                     for (c0, nc, _, _), copies in zip(c.gather_parts, c.gather_copies):
                         _lib.call("ha_adamw_step", c.table.ptr, chunks.data_ptr() + c0 * _lib.CHUNK_DTYPE.itemsize,
@@ -960,20 +1036,31 @@ class ZeroOneAdamW:
             for st in self._gather_streams:
                 main.wait_stream(st)
             self._phase("adamw", False)
+            # a dirty tensor without a gradient is not updated, but the reference still broadcasts
+            # every parameter from its owner (optimizer.py:192-194): do the same with one all-gather
+            regather = self.world > 1 and bool((self._dirty & ~updated).any())
             if p2p:
                 self._phase("barrier", True)
                 self._barrier()  # peers use their parameters only after every rank's stores landed
                 self._phase("barrier", False)
+                if regather:
+                    self._all_gather_params()
                 if self._land_hooks:  # every owner has read its windows: early pushes may start
                     self._window_free = torch.cuda.Event()
                     self._window_free.record()
                     self._land_ok = True
             elif self.world > 1:
-                self._phase("all_gather", True)
-                for c in self._classes:
-                    own = c.packed_param.data_ptr() + self.rank * c.layout.seg_len * c.packed_param.element_size()
-                    self._comm.all_gather(own, c.packed_param.data_ptr(), c.layout.seg_len, c.code)
-                self._phase("all_gather", False)
+                self._all_gather_params()
+            # written in full (dense) or by changed groups from a clean state: clean now, on every rank
+            self._dirty &= ~updated
+
+    def _all_gather_params(self) -> None:
+        """Every rank's packed parameter segments from their owners (NCCL, in place)."""
+        self._phase("all_gather", True)
+        for c in self._classes:
+            own = c.packed_param.data_ptr() + self.rank * c.layout.seg_len * c.packed_param.element_size()
+            self._comm.all_gather(own, c.packed_param.data_ptr(), c.layout.seg_len, c.code)
+        self._phase("all_gather", False)
 
     def state_summary(self) -> str:
         """optimizer.py:196-199."""

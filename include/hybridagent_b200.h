@@ -222,6 +222,16 @@ int ha_adamw_step_peers(const ha_tensor* d_tensors, const ha_chunk* d_chunks, in
                         int64_t chunk_elems, int grad_dtype, int param_dtype, const ha_adamw_scalars* scalars,
                         const ha_peers* peers, void* stream);
 
+/* ha_adamw_step for 16-bit parameters (param_dtype HA_BF16 or HA_F16, the gradient of the
+ * same type) that stores a 4-element group of the parameter copy only where its rounded value
+ * changes -- the `param.copy_(master.to(param.dtype))` of optimizer.py:191 -- and, with
+ * `peers` non-NULL, stores those groups also into every peer's packed parameter buffer (the
+ * broadcast of optimizer.py:192-194).  The caller guarantees that on entry every copy of each
+ * parameter (local and peers') equals RNE(master); the result is then bit for bit that of a
+ * full write on every copy, while unchanged groups cost no HBM write and no NVLink bytes. */
+int ha_adamw_step_delta(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks, int64_t chunk_elems,
+                        int param_dtype, const ha_adamw_scalars* sc, const ha_peers* peers, void* stream);
+
 /* ------------------------------------------------------------------ NCCL (NVLink / NVSwitch) */
 
 typedef struct ha_comm ha_comm;

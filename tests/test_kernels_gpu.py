@@ -241,13 +241,15 @@ def test_gather(elem, how):
                            want.view(torch.int16 if elem == 2 else torch.int32)), k
 
 
+@pytest.mark.parametrize("entry", ["delta_peers", "delta_local", "dense_peers"])
 @pytest.mark.parametrize("code", [BF16, F16], ids=["bf16", "f16"])
-def test_adamw_peers_store_changed_groups_only(code):
-    """ha_adamw_step_peers with two 'peers' emulated on this GPU (arenas at fixed offsets from
-    the local parameter arena).  Local parameters and every peer end with the oracle's new
-    values wherever a 4-element group (per element on the scalar path and ragged tails)
-    changed; unchanged groups are not stored at all -- a sentinel planted in a peer's copy of an
-    unchanged group survives, one in a changed group is overwritten."""
+def test_adamw_peer_and_changed_group_stores(code, entry):
+    """Parameter stores of the fused update, with two 'peers' emulated on this GPU (arenas at
+    fixed offsets from the local parameter arena).  ha_adamw_step_delta: the local parameters
+    (and, with peers, every peer) end with the oracle's new values wherever a 4-element group
+    (per element on the scalar path and ragged tails) changed its rounded value; unchanged
+    groups are not stored at all -- a sentinel planted in a peer's copy of an unchanged group
+    survives, one in a changed group is overwritten.  ha_adamw_step_peers stores every group."""
     import torch
     sizes = SIZES + [3 * 16384 + 6]
     n = len(sizes)
@@ -283,8 +285,12 @@ def test_adamw_peers_store_changed_groups_only(code):
     dchunks = _dev_bytes(chunks)
     sc = _lib.AdamwScalars()
     _lib.call("ha_make_scalars", B1, B2, EPS, 0.01, code, 0, 0.0, ctypes.byref(sc))
-    _lib.call("ha_adamw_step_peers", table.data_ptr(), dchunks.data_ptr(), len(chunks), _lib.HA_ADAMW_CHUNK, code, code,
-              ctypes.byref(sc), ctypes.byref(pe), _stream())
+    if entry == "dense_peers":
+        _lib.call("ha_adamw_step_peers", table.data_ptr(), dchunks.data_ptr(), len(chunks), _lib.HA_ADAMW_CHUNK, code,
+                  code, ctypes.byref(sc), ctypes.byref(pe), _stream())
+    else:
+        _lib.call("ha_adamw_step_delta", table.data_ptr(), dchunks.data_ptr(), len(chunks), _lib.HA_ADAMW_CHUNK, code,
+                  ctypes.byref(sc), ctypes.byref(pe) if entry == "delta_peers" else None, _stream())
     torch.cuda.synchronize()
     got_local = to_numpy(local, code)
     got_peers = [to_numpy(p, code) for p in peers]
@@ -302,14 +308,19 @@ def test_adamw_peers_store_changed_groups_only(code):
         # an aligned tensor), or the element itself (scalar path, ragged tail)
         diff = param != old
         stored = diff.copy()
-        if ts.np_grad[k] is not None and k not in (4, 13):
+        if entry == "dense_peers":
+            stored[:] = ts.np_grad[k] is not None
+        elif ts.np_grad[k] is not None and k not in (4, 13):
             full = size // 4 * 4
             grp = diff[:full].reshape(-1, 4).any(axis=1)
             stored[:full] = np.repeat(grp, 4)
+        if entry == "delta_local":
+            stored[:] = False  # no peer is written
         changed_any += int(diff.sum())
         for q in range(2):
             want = np.where(stored, param, peer_init[q][sl])
             assert_bits_equal(got_peers[q][sl], want, f"peer {q} param[{k}]")
     assert changed_any > 1000  # the large-lr tensors moved
-    survived = int((got_peers[0][planted] == peer_init[0][planted]).sum())
-    assert survived > 1000  # most sentinels sat in unchanged groups of the tiny-lr tensors
+    if entry != "dense_peers":
+        survived = int((got_peers[0][planted] == peer_init[0][planted]).sum())
+        assert survived > 1000  # most sentinels sat in unchanged groups of the tiny-lr tensors

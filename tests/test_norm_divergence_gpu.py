@@ -10,9 +10,10 @@ reference's own op sequence run by torch on the same GPU with its own fp32 norm
 (oracle/torch_ops.py), and -- for scale -- the same reference run on the CPU against itself on
 the GPU.  The counts are printed as one ``NORM-DIVERGENCE`` JSON line (``pytest -s``).
 
-Asserted: the norms agree to 1e-6; where a step's two fp32 norms are equal, every state bit
-and parameter is equal; the product never differs from the reference on CUDA in more
-elements than the reference on the CPU does."""
+Asserted: the norms agree to 1e-6; where every step's two fp32 norms are equal, every state
+bit and parameter is equal; and per state array the product has no more elements outside the
+parity criterion against the reference on CUDA than the reference on the CPU has against itself
+on CUDA, or at most 1e-4 of the elements (the measured count is in the printed line)."""
 import json
 import math
 
@@ -23,13 +24,13 @@ from helpers import Z, to_numpy, to_torch
 
 pytestmark = pytest.mark.gpu
 
-STEPS = 4
+STEPS = 8
 
 
 def _slice():
     from hybridagent_b200 import workloads
     shapes = workloads.qwen3_14b()
-    # two decoder layers (q/k/v/o, gate/up/down, norms): ~0.8 B... cut to ~60 M parameters
+    # the leading tensors of the first decoder layer, up to 60 M parameters
     return workloads.truncated(shapes, 60_000_000)
 
 

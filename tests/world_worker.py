@@ -198,6 +198,12 @@ def main(name: str, out_dir: str) -> None:
         else:
             for p, g, shape in zip(params, case.grads(s, rank), case.shapes):
                 p.grad = None if g is None else to_torch(g, case.dtype, shape, dev)
+        if os.environ.get("WORKER_DIRTY") == "1" and s == 1 and rank == world - 1:
+            # this rank overwrites its copy of a tensor another rank owns: the next step must
+            # restore the owner's values everywhere (the reference's broadcast does)
+            j = next(i for i in range(len(params)) if opt.owner[i] != rank)
+            with torch.no_grad():
+                params[j].copy_(torch.zeros_like(params[j]))
         opt.all_reduce_grads()
         grads_seen.append({i: None if p.grad is None else to_numpy(p.grad, case.dtype) for i, p in enumerate(params)})
         n = opt.clip_grad_norm(case.max_norm)
@@ -207,6 +213,7 @@ def main(name: str, out_dir: str) -> None:
     torch.cuda.synchronize()
     result = {
         "rank": rank, "norms": norms, "owner": opt.owner, "mode": opt.comm_mode, "land_launches": opt.land_launches,
+        "dense_steps": opt.dense_steps,
         "params": [to_numpy(p.data, case.dtype) for p in params],
         "state": {i: (to_numpy(opt.master[i], 0), to_numpy(opt.exp_avg[i], 0), to_numpy(opt.exp_avg_sq[i], 0),
                       opt.param_steps[i]) for i in opt.param_steps},
