@@ -54,7 +54,10 @@ ALGO_BYTES_SUMSQ = {"bf16": 2, "f16": 2, "f32": 4}
 FALLBACK_HBM_GBS = 6650.0
 RECIPE_NVLINK_GBS = 770.0   # the pool's published peer-copy figure, used only where no probe of ours exists
 NOMINAL_NVLINK_GBS = 900.0  # NVLink 5, per direction per GPU
-TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "adamw_kernel_qwen3_8b.json")
+# ncu DRAM bytes per parameter of one update launch: full writes of the bf16 copy, and writes of
+# the changed groups only
+TRAFFIC_PROFILES = {"full": os.path.join(ROOT, "profiles", "adamw_kernel_qwen3_8b.json"),
+                    "changed groups": os.path.join(ROOT, "profiles", "adamw_delta_kernel_qwen3_8b.json")}
 LINK_PROFILE = os.path.join(ROOT, "profiles", "nvlink_peak.json")
 
 
@@ -463,13 +466,15 @@ def measured_hbm_peak() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic_per_param() -> float | None:
-    """DRAM bytes per owned parameter of one AdamW launch, from the committed ncu record."""
+def profiled_traffic_per_param(mode: str) -> tuple[float | None, str | None]:
+    """DRAM bytes per owned parameter of one AdamW launch writing the parameter copies in
+    ``mode``, from the committed ncu record, and the record's path."""
+    path = TRAFFIC_PROFILES[mode]
     try:
-        with open(TRAFFIC_PROFILE) as f:
-            return float(json.load(f)["traffic_bytes_per_param"])
+        with open(path) as f:
+            return float(json.load(f)["traffic_bytes_per_param"]), os.path.relpath(path, ROOT)
     except (OSError, KeyError, ValueError):
-        return None
+        return None, None
 
 
 def measured_link_peak(world: int) -> tuple[float, str]:
@@ -568,6 +573,7 @@ def run_ours(args) -> None:
         barrier()
         timer.enabled = False
     launches = opt.launches - launches0
+    writes = opt.write_stats()  # how the last timed update wrote the parameter copies
     ms = start.elapsed_time(stop) / args.steps
     phases = timer.per_step_ms(args.steps)
     t = torch.tensor([ms, phases.get("adamw", 0.0)], dtype=torch.float64, device=dev)
@@ -660,10 +666,15 @@ def run_ours(args) -> None:
         return
     peak, peak_kind = measured_hbm_peak()
     adamw_ms = phases.get("adamw")
-    algo = ALGO_BYTES_ADAMW["bf16"] * owned_params
+    # the update reads grad + master/m/v and writes master/m/v (26 B per owned param); the bf16 copy
+    # costs 2 B per param when written in full, else 8 B per changed 4-element group
+    delta = writes["mode"] == "changed groups"
+    algo = (26 * owned_params + 8 * writes["changed_groups"]) if delta else ALGO_BYTES_ADAMW["bf16"] * owned_params
     achieved = algo / (adamw_ms * 1e-3) / 1e9 if adamw_ms else None
-    tpp = profiled_traffic_per_param()
-    hbm_roof = {"bound": "hbm", "kernel": f"adamw_kernel<{'f32' if fp32_set else 'bf16'}>",
+    tpp, tpp_src = profiled_traffic_per_param(writes["mode"])
+    hbm_roof = {"bound": "hbm", "kernel": f"adamw_kernel<{'f32' if fp32_set else 'bf16'}>" +
+                (" (changed groups of the bf16 copy)" if delta else ""),
+                "param_writes": writes,
                 "achieved": None if achieved is None else round(achieved, 1),
                 "peak": peak, "unit": "GB/s",
                 "frac": None if achieved is None else round(achieved / peak, 4),
@@ -671,8 +682,8 @@ def run_ours(args) -> None:
                 else "fallback 6.65 TB/s",
                 "algorithmic_bytes_per_launch": algo,
                 "traffic": None if tpp is None else round(tpp * owned_params),
-                "traffic_source": None if tpp is None else "ncu dram__bytes_read+write per parameter of one launch "
-                "(profiles/adamw_kernel_qwen3_8b.json), times this launch's parameters"}
+                "traffic_source": None if tpp is None else f"ncu dram__bytes_read+write per parameter of one launch "
+                f"({tpp_src}), times this launch's parameters"}
     roofline, nvlink = hbm_roof, None
     if world > 1 and opt.comm_mode == "p2p":
         # per phase: its HBM bytes and the bytes it moves over NVLink per GPU; the phase is bound by
@@ -689,10 +700,11 @@ def run_ours(args) -> None:
                     "gather_kernel peer stores")
         if opt.gather_mode == "ce":
             gather_how, moved = "adamw_kernel<bf16> in parts + copy-engine all-gather", 1.0
+        elif delta:
+            gather_how = "adamw_kernel<bf16, PEERS, DELTA>: stores of the changed 4-element groups, fused"
+            moved = writes["changed_groups"] / max(writes["groups"], 1)
         else:
-            p = parity["changed_param_fraction"] if parity else 1.0
-            gather_how = "adamw_kernel<bf16, PEERS>: peer stores of the changed 4-element groups, fused"
-            moved = 1.0 - (1.0 - p) ** 4
+            gather_how, moved = "adamw_kernel<bf16, PEERS>: every group stored into every peer, fused", 1.0
         adamw_link = int(2 * owned_params * (world - 1) * moved)
         nvlink = {"link_peak_gbs": link, "link_peak_source": link_src, "nominal_gbs": NOMINAL_NVLINK_GBS,
                   "all_gather_fraction_moved": round(moved, 6)}

@@ -77,7 +77,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "ha_sum_regions": ([_vp, _i32, _i64, _i64, _vp, ctypes.c_int, _vp, _vp, _vp], ctypes.c_int),
     "ha_adamw_step_peers": ([_vp, _vp, _i64, _i64, ctypes.c_int, ctypes.c_int, ctypes.POINTER(AdamwScalars),
                              ctypes.POINTER(Peers), _vp], ctypes.c_int),
-    "ha_adamw_step_delta": ([_vp, _vp, _i64, _i64, ctypes.c_int, ctypes.POINTER(AdamwScalars), _vp, _vp],
+    "ha_adamw_step_delta": ([_vp, _vp, _i64, _i64, ctypes.c_int, ctypes.POINTER(AdamwScalars), _vp, _vp, _vp],
                             ctypes.c_int),
     "ha_comm_unique_id": ([_vp], ctypes.c_int),
     "ha_comm_init": ([_vp, _i32, _i32, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),

@@ -105,11 +105,16 @@ __device__ __forceinline__ void push1(const Peers& p, uint64_t local, int64_t k,
 // full write would leave.  With the small learning rates of RL fine-tuning few bf16 values move
 // in a step, so this saves the 2 B/param parameter write in HBM and nearly all of the
 // all-gather's NVLink bytes.
+//
+// `changed` (DELTA, may be null): the number of stored groups (scalar-path elements count as
+// groups) is added to it, one atomic per CTA, so the caller can tell how much moved.
 template <int DT, bool PEERS, bool DELTA>
 __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __restrict__ tensors,
-                                                         const ha_chunk* __restrict__ chunks, Scalars s, Peers peers) {
+                                                         const ha_chunk* __restrict__ chunks, Scalars s, Peers peers,
+                                                         unsigned long long* changed) {
   static_assert(!(DELTA && DT == HA_F32), "fp32 parameters are their own masters: always written");
   __shared__ StagedChunk sc;
+  __shared__ uint32_t stored_in_cta;
   stage_chunk(tensors, chunks, &sc);
   const ha_tensor& t = sc.t;
   if (t.grad == 0) return;  // no gradient: skipped entirely (optimizer.py:174)
@@ -126,6 +131,8 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
   constexpr uint64_t kNarrowAlign = DT == HA_F32 ? 15 : 7;
   const bool vec = ((t.master | t.exp_avg | t.exp_avg_sq) & 15) == 0 && (t.grad & kNarrowAlign) == 0 &&
                    (DT == HA_F32 || (t.param & kNarrowAlign) == 0);
+  uint32_t stored = 0;  // DELTA: groups this thread stored
+  if (DELTA && threadIdx.x == 0) stored_in_cta = 0;
   // one element on the scalar paths (ragged tails, unaligned tensors)
   auto one = [&](int64_t k) {
     float a = master[k], b = exp_avg[k], c = exp_avg_sq[k];
@@ -139,6 +146,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
       if (!DELTA || w != Elem<DT>::narrow(before)) {
         static_cast<uint16_t*>(param)[k] = w;
         if constexpr (PEERS) push1<DT>(peers, pushed, k, a);
+        stored += DELTA;
       }
     } else if constexpr (PEERS) {
       push1<DT>(peers, pushed, k, a);
@@ -175,6 +183,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
             if (!DELTA || w.x != before.x || w.y != before.y) {
               __stcs(reinterpret_cast<uint2*>(static_cast<uint16_t*>(param) + e[u]), w);
               if constexpr (PEERS) push_raw4(peers, pushed, e[u], w);
+              stored += DELTA;
             }
           } else if constexpr (PEERS) {
             push_f32x4(peers, pushed, e[u], ms[u]);
@@ -186,6 +195,16 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
     }
   } else {
     for (int64_t k = begin + threadIdx.x; k < end; k += kThreads) one(k);
+  }
+  if constexpr (DELTA) {
+    if (changed != nullptr) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) stored += __shfl_xor_sync(0xffffffffu, stored, o);
+      __syncthreads();  // stored_in_cta was cleared before any thread adds to it
+      if ((threadIdx.x & 31) == 0 && stored) atomicAdd(&stored_in_cta, stored);
+      __syncthreads();
+      if (threadIdx.x == 0 && stored_in_cta) atomicAdd(changed, static_cast<unsigned long long>(stored_in_cta));
+    }
   }
 }
 
@@ -231,9 +250,9 @@ extern "C" int ha_adamw_step(const ha_tensor* d_tensors, const ha_chunk* d_chunk
   const dim3 grid(static_cast<unsigned>(n_chunks));
   const Peers none{};
   switch (grad_dtype) {
-    case HA_F32: adamw_kernel<HA_F32, false, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none); break;
-    case HA_BF16: adamw_kernel<HA_BF16, false, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none); break;
-    default: adamw_kernel<HA_F16, false, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none); break;
+    case HA_F32: adamw_kernel<HA_F32, false, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none, nullptr); break;
+    case HA_BF16: adamw_kernel<HA_BF16, false, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none, nullptr); break;
+    default: adamw_kernel<HA_F16, false, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, none, nullptr); break;
   }
   return check_launch("adamw_kernel");
 }
@@ -263,16 +282,16 @@ extern "C" int ha_adamw_step_peers(const ha_tensor* d_tensors, const ha_chunk* d
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid(static_cast<unsigned>(n_chunks));
   switch (grad_dtype) {
-    case HA_F32: adamw_kernel<HA_F32, true, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p); break;
-    case HA_BF16: adamw_kernel<HA_BF16, true, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p); break;
-    default: adamw_kernel<HA_F16, true, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p); break;
+    case HA_F32: adamw_kernel<HA_F32, true, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p, nullptr); break;
+    case HA_BF16: adamw_kernel<HA_BF16, true, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p, nullptr); break;
+    default: adamw_kernel<HA_F16, true, false><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p, nullptr); break;
   }
   return check_launch("adamw_kernel (peers)");
 }
 
 extern "C" int ha_adamw_step_delta(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,
                                    int64_t chunk_elems, int param_dtype, const ha_adamw_scalars* sc,
-                                   const ha_peers* peers, void* stream) {
+                                   const ha_peers* peers, unsigned long long* d_changed_groups, void* stream) {
   HA_NVTX_RANGE();
   using namespace ha;
   if (chunk_elems != HA_ADAMW_CHUNK)
@@ -299,12 +318,13 @@ extern "C" int ha_adamw_step_delta(const ha_tensor* d_tensors, const ha_chunk* d
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid(static_cast<unsigned>(n_chunks));
   const bool with_peers = peers != nullptr && p.n > 0;
+  unsigned long long* cnt = d_changed_groups;
   if (param_dtype == HA_BF16) {
-    if (with_peers) adamw_kernel<HA_BF16, true, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p);
-    else adamw_kernel<HA_BF16, false, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p);
+    if (with_peers) adamw_kernel<HA_BF16, true, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p, cnt);
+    else adamw_kernel<HA_BF16, false, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p, cnt);
   } else {
-    if (with_peers) adamw_kernel<HA_F16, true, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p);
-    else adamw_kernel<HA_F16, false, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p);
+    if (with_peers) adamw_kernel<HA_F16, true, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p, cnt);
+    else adamw_kernel<HA_F16, false, true><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, s, p, cnt);
   }
   return check_launch("adamw_kernel (delta)");
 }

@@ -217,6 +217,15 @@ class _Class:
         self.partials = torch.empty(max(self.sumsq_chunks[1], 1), dtype=torch.float64, device=dev)
         self.move = None
         self.peers = _lib.Peers()
+        # changed-groups-only writes: the groups stored by the last such update (device counter,
+        # read back without waiting) decide whether the next update is one too
+        self.changed_dev = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.changed_host = torch.zeros(1, dtype=torch.int64, pin_memory=True)
+        self.changed_event: torch.cuda.Event | None = None
+        self.delta_next = True
+        self.full_run = 0  # consecutive full updates chosen by the count (a changed-groups one is tried after 8)
+        self.last_changed: int | None = None
+        self.groups = sum((numel[i] + 3) // 4 for i in self.owned)  # 4-element groups owned
 
     def set_mode(self, opt: "ZeroOneAdamW", recv_bases: list[int] | None, param_bases: list[int] | None) -> None:
         """p2p (peers' receive windows and parameter buffers mapped) or the local nccl pack.
@@ -392,6 +401,12 @@ class ZeroOneAdamW:
         # parameter or a master; such tensors are "dirty" (the same set on every rank) and the
         # next step writes every parameter in full, as the reference does.
         self.delta_writes = os.environ.get("HYBRIDAGENT_B200_DELTA", "1") != "0"
+        # above this fraction of changed groups (last update) the next update writes in full: with
+        # most groups changing, scattered stores cost more than a full one (measured on B200 at one
+        # GPU: 0.5 % changed -> 6 % faster than the full write, ~90 % changed -> 29 % slower)
+        self.delta_max_fraction = float(os.environ.get("HYBRIDAGENT_B200_DELTA_MAX_FRACTION",
+                                                       "0.05" if self.world == 1 else "0.1"))
+
         self._dirty = np.zeros(len(self.params), dtype=bool)
         self._force_dirty = np.zeros(len(self.params), dtype=bool)
         self._seen_params = self._param_versions()
@@ -1010,10 +1025,24 @@ class ZeroOneAdamW:
             main = torch.cuda.current_stream()
             for c, sc in launches:
                 chunks, n = c.adamw_chunks
-                if n and not dense and c.code != HA_F32 and not ce_gather and self.comm_mode != "nccl":
+                if c.changed_event is not None and c.changed_event.query():  # the last count has landed
+                    c.last_changed = int(c.changed_host[0])
+                    c.delta_next = c.last_changed <= self.delta_max_fraction * max(c.groups, 1)
+                    c.changed_event = None
+                elif not c.delta_next:
+                    c.full_run += 1
+                    if c.full_run >= 8:  # look again: the learning rate or the gradients may have changed
+                        c.delta_next, c.full_run = True, 0
+                if (n and not dense and c.delta_next and c.code != HA_F32 and not ce_gather
+                        and self.comm_mode != "nccl"):
+                    _lib.call("ha_memset", c.changed_dev.data_ptr(), 0, 8, self._stream())
                     _lib.call("ha_adamw_step_delta", c.table.ptr, chunks.data_ptr(), n, HA_ADAMW_CHUNK, c.code,
-                              ctypes.byref(sc), ctypes.byref(c.peers) if p2p else None, self._stream())
+                              ctypes.byref(sc), ctypes.byref(c.peers) if p2p else None, c.changed_dev.data_ptr(),
+                              self._stream())
                     self.launches += 1
+                    c.changed_host.copy_(c.changed_dev, non_blocking=True)
+                    c.changed_event = torch.cuda.Event()
+                    c.changed_event.record()
                 elif n and ce_gather:  # update in parts; the copy engines send each finished part to the peers
                     esz = c.packed_param.element_size()
                     for (c0, nc, _, _), copies in zip(c.gather_parts, c.gather_copies):
@@ -1053,6 +1082,28 @@ class ZeroOneAdamW:
                 self._all_gather_params()
             # written in full (dense) or by changed groups from a clean state: clean now, on every rank
             self._dirty &= ~updated
+
+    def write_stats(self) -> dict:
+        """How the parameter copies were written by the latest update: ``mode`` ("changed groups"
+        or "full"), ``changed_groups`` (4-element groups stored by the latest changed-groups
+        update, all classes; waits for its count) and ``groups`` (4-element groups owned)."""
+        for c in self._classes:
+            if c.changed_event is not None:
+                c.changed_event.synchronize()
+                c.last_changed = int(c.changed_host[0])
+                c.delta_next = c.last_changed <= self.delta_max_fraction * max(c.groups, 1)
+                c.changed_event = None
+        bf = [c for c in self._classes if c.code != HA_F32]
+        delta = bool(bf) and not self._dense_this_step and all(c.last_changed is not None for c in bf)
+        return {"mode": "changed groups" if delta else "full", "changed_groups": self.last_changed_groups,
+                "groups": sum(c.groups for c in bf)}
+
+    @property
+    def last_changed_groups(self) -> int | None:
+        """4-element parameter groups stored by the most recent changed-groups update whose
+        count has been read back (all classes), or None before the first."""
+        counts = [c.last_changed for c in self._classes if c.last_changed is not None]
+        return sum(counts) if counts else None
 
     def _all_gather_params(self) -> None:
         """Every rank's packed parameter segments from their owners (NCCL, in place)."""

@@ -289,9 +289,11 @@ def test_adamw_peer_and_changed_group_stores(code, entry):
         _lib.call("ha_adamw_step_peers", table.data_ptr(), dchunks.data_ptr(), len(chunks), _lib.HA_ADAMW_CHUNK, code,
                   code, ctypes.byref(sc), ctypes.byref(pe), _stream())
     else:
+        cnt = torch.zeros(1, dtype=torch.int64, device="cuda")
         _lib.call("ha_adamw_step_delta", table.data_ptr(), dchunks.data_ptr(), len(chunks), _lib.HA_ADAMW_CHUNK, code,
-                  ctypes.byref(sc), ctypes.byref(pe) if entry == "delta_peers" else None, _stream())
+                  ctypes.byref(sc), ctypes.byref(pe) if entry == "delta_peers" else None, cnt.data_ptr(), _stream())
     torch.cuda.synchronize()
+    want_count = 0
     got_local = to_numpy(local, code)
     got_peers = [to_numpy(p, code) for p in peers]
     changed_any = 0
@@ -314,6 +316,9 @@ def test_adamw_peer_and_changed_group_stores(code, entry):
             full = size // 4 * 4
             grp = diff[:full].reshape(-1, 4).any(axis=1)
             stored[:full] = np.repeat(grp, 4)
+            want_count += int(grp.sum()) + int(diff[full:].sum())
+        elif ts.np_grad[k] is not None:
+            want_count += int(diff.sum())  # scalar path: one per changed element
         if entry == "delta_local":
             stored[:] = False  # no peer is written
         changed_any += int(diff.sum())
@@ -322,5 +327,6 @@ def test_adamw_peer_and_changed_group_stores(code, entry):
             assert_bits_equal(got_peers[q][sl], want, f"peer {q} param[{k}]")
     assert changed_any > 1000  # the large-lr tensors moved
     if entry != "dense_peers":
+        assert int(cnt.item()) == want_count  # the groups the kernel counts as stored
         survived = int((got_peers[0][planted] == peer_init[0][planted]).sum())
         assert survived > 1000  # most sentinels sat in unchanged groups of the tiny-lr tensors
