@@ -443,6 +443,10 @@ class ZeroOneAdamW:
         # the push kernel stores instead, using SM time the local copies and sums leave idle and
         # link bandwidth the copy engines leave unused (world 2: 0.1 -> 32.4 ms, 0 -> 33.0, 0.2 -> 32.7)
         self.push_kernel_share = float(os.environ.get("HYBRIDAGENT_B200_PUSH_KERNEL_SHARE", "0.1"))
+        # the push kernel's grid: 0 -- one CTA per 16384-element chunk (every SM busy pushing);
+        # N > 0 -- N CTAs walking the round's chunk list, each with 4 vectors per thread in
+        # flight, leaving the other SM slots to the owner sums of the previous round
+        self.push_ctas = int(os.environ.get("HYBRIDAGENT_B200_PUSH_CTAS", "0"))
         # the parameter all-gather (p2p): "kernel" -- the update kernel stores every new value into
         # every peer's copy; "ce" -- the update runs in parts of HYBRIDAGENT_B200_GATHER_PART_BYTES and
         # the copy engines send each finished part to every peer (one stream per peer) while the
@@ -515,8 +519,12 @@ class ZeroOneAdamW:
             for c in self._classes:
                 if k < c.pieces.n_rounds and c.round_chunks[k][1]:
                     ch, n = c.round_chunks[k]
-                    _lib.call("ha_gather", c.move.ptr, ch.data_ptr(), n, HA_ADAMW_CHUNK,
-                              c.packed_param.element_size(), main.cuda_stream)
+                    if self.push_ctas > 0:
+                        _lib.call("ha_gather_capped", c.move.ptr, ch.data_ptr(), n, HA_ADAMW_CHUNK,
+                                  c.packed_param.element_size(), self.push_ctas, main.cuda_stream)
+                    else:
+                        _lib.call("ha_gather", c.move.ptr, ch.data_ptr(), n, HA_ADAMW_CHUNK,
+                                  c.packed_param.element_size(), main.cuda_stream)
                     self.launches += 1
             for st in self._push_streams:
                 main.wait_stream(st)
@@ -858,6 +866,24 @@ class ZeroOneAdamW:
                     keep.append(g)
                     ptrs[k] = g.data_ptr()
                 class_ptrs.append(ptrs)
+            # the copy tables depend only on this rank's gradients (a tensor no rank uses has no
+            # gradient here either: zero-filled, optimizer.py:111-114), so they are built and
+            # uploaded before the mask's all-reduce and the host waits only for that
+            for ci, (c, ptrs) in enumerate(zip(self._classes, class_ptrs)):
+                if p2p:  # each piece reads its part of its tensor's gradient (0: zero-fill; gaps: zeros)
+                    done = None
+                    if landed:  # pieces pushed while their gradient landed, gradient unchanged: skipped
+                        done = np.zeros(len(c.layout.indices), dtype=bool)
+                        for i, (g, version) in landed.items():
+                            # the same object, not modified in place since its push (in-place ops
+                            # such as p.grad.div_() bump the version counter)
+                            if self._entry_of[i][0] == ci and self.params[i].grad is g and g._version == version:
+                                done[self._entry_of[i][1]] = True
+                    src = layout.piece_sources(c.pieces, ptrs, c.packed_param.element_size(), c.piece_dst, done)
+                    c.move.np["src"][:len(src)] = src
+                else:  # equal to dst when the gradient already lives in its slot
+                    c.move.np["src"][:len(ptrs)] = ptrs
+                c.move.upload()
             T = len(self.params)
             local[T:] = self._detect_dirty()  # every rank learns every rank's dirty tensors
             self._used_dev.copy_(self._used_local, non_blocking=True)  # no host wait: a peer may be missing
@@ -873,22 +899,6 @@ class ZeroOneAdamW:
                 self._land_waited = False
                 self._land_ok = False  # until the update's barrier frees the windows again
                 self._landed = {}
-            for ci, (c, ptrs) in enumerate(zip(self._classes, class_ptrs)):
-                ptrs[~used[np.asarray(c.layout.indices)]] = 0  # unused everywhere: zeros (optimizer.py:111-114)
-                if p2p:  # each piece reads its part of its tensor's gradient (0: zero-fill; gaps: zeros)
-                    done = None
-                    if landed:  # pieces pushed while their gradient landed, gradient unchanged: skipped
-                        done = np.zeros(len(c.layout.indices), dtype=bool)
-                        for i, (g, version) in landed.items():
-                            # the same object, not modified in place since its push (in-place ops
-                            # such as p.grad.div_() bump the version counter)
-                            if self._entry_of[i][0] == ci and self.params[i].grad is g and g._version == version:
-                                done[self._entry_of[i][1]] = True
-                    src = layout.piece_sources(c.pieces, ptrs, c.packed_param.element_size(), c.piece_dst, done)
-                    c.move.np["src"][:len(src)] = src
-                else:  # equal to dst when the gradient already lives in its slot
-                    c.move.np["src"][:len(ptrs)] = ptrs
-                c.move.upload()
             if p2p:
                 self._exchange_rounds()
             else:
