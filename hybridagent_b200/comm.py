@@ -45,10 +45,11 @@ class CommFailure(RuntimeError):
     stopped participating); the communicator has been aborted."""
 
 
-def poll(done, deadline_s: float, on_timeout, spin_s: float = 0.002, nap_s: float = 0.0002) -> bool:
+def poll(done, deadline_s: float, on_timeout, spin_s: float = 0.005, nap_s: float = 0.00005) -> bool:
     """Waits until ``done()`` is true; returns False (after calling ``on_timeout()``) if it is
-    still false after ``deadline_s`` seconds.  Spins for ``spin_s`` (the common, short
-    case), then naps ``nap_s`` between checks; never blocks inside a CUDA call."""
+    still false after ``deadline_s`` seconds.  Spins for ``spin_s``, then naps ``nap_s``
+    between checks (the GPU idles from the moment the awaited work ends until this returns and
+    the caller launches the next, so the nap is short); never blocks inside a CUDA call."""
     t0 = time.monotonic()
     while not done():
         dt = time.monotonic() - t0

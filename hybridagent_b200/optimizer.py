@@ -445,8 +445,12 @@ class ZeroOneAdamW:
         self.push_kernel_share = float(os.environ.get("HYBRIDAGENT_B200_PUSH_KERNEL_SHARE", "0.1"))
         # the push kernel's grid: 0 -- one CTA per 16384-element chunk (every SM busy pushing);
         # N > 0 -- N CTAs walking the round's chunk list, each with 4 vectors per thread in
-        # flight, leaving the other SM slots to the owner sums of the previous round
-        self.push_ctas = int(os.environ.get("HYBRIDAGENT_B200_PUSH_CTAS", "0"))
+        # flight, leaving the other SM slots to the owner sums of the previous round.  Measured
+        # on B200 at world 2 (kernel push of every piece): one CTA per chunk 34.4 ms per step (the
+        # starved sums of the last rounds stay exposed), 148 CTAs 32.1, 296 31.1, 592 31.0.  With
+        # the copy-engine push the kernel only copies this rank's own pieces: one CTA per chunk
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.push_ctas = int(os.environ.get("HYBRIDAGENT_B200_PUSH_CTAS", str(4 * sms if self.push_streams == 0 else 0)))
         # the parameter all-gather (p2p): "kernel" -- the update kernel stores every new value into
         # every peer's copy; "ce" -- the update runs in parts of HYBRIDAGENT_B200_GATHER_PART_BYTES and
         # the copy engines send each finished part to every peer (one stream per peer) while the
