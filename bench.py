@@ -699,7 +699,8 @@ def run_ours(args) -> None:
         foreign = n_params - owned_params
         push_how = ("copy engines, one stream per peer" if opt.push_streams < 0 else
                     f"copy engines on {opt.push_streams} streams + gather_kernel" if opt.push_streams > 0 else
-                    "gather_kernel peer stores")
+                    f"gather_capped_kernel peer stores on {opt.push_ctas} CTAs" if opt.push_ctas > 0 else
+                    "gather_kernel peer stores, one CTA per chunk")
         if opt.gather_mode == "ce":
             gather_how, moved = "adamw_kernel<bf16> in parts + copy-engine all-gather", 1.0
         elif delta:

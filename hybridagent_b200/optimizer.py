@@ -132,6 +132,7 @@ class _ParamSteps(MutableMapping):
         self._counts = counts
         self._owned = set(owned)
         self._order = list(owned)
+        self.version = 0
 
     def __getitem__(self, i: int) -> int:
         if i not in self._owned:
@@ -142,6 +143,7 @@ class _ParamSteps(MutableMapping):
         if i not in self._owned:
             raise KeyError(f"tensor {i} is not owned by this rank")
         self._counts[i] = int(v)
+        self.version += 1  # tables staged with the old counts are stale
 
     def __delitem__(self, i: int) -> None:
         raise TypeError("param_steps entries cannot be removed")
@@ -371,6 +373,8 @@ class ZeroOneAdamW:
             self.exp_avg: dict[int, torch.Tensor] = {}
             self.exp_avg_sq: dict[int, torch.Tensor] = {}
             self._steps = np.zeros(len(self.params), dtype=np.int64)
+            self._table_epoch = 0  # table uploads so far (a staged table is valid while it is the last)
+            self._staged = None
             owned_all = [i for i in range(len(self.params)) if self.owner[i] == self.rank]
             self.param_steps = _ParamSteps(self._steps, owned_all)
             self.owned_numel = sum(self._numels[i] for i in owned_all)
@@ -645,6 +649,10 @@ class ZeroOneAdamW:
         return grads, ptrs
 
     def _upload_table(self, c: _Class, grad_ptrs: np.ndarray, advance: bool) -> None:
+        """Uploads class c's tensor table: the gradient pointers and, with ``advance``, the
+        scalars of the next update (each tensor with a gradient at its step count + 1,
+        optimizer.py:181); the counts themselves advance only when step() runs."""
+        self._table_epoch += 1
         tab = c.table.np[:len(c.owned)]
         tab["grad"] = grad_ptrs
         if c.code != HA_F32 and self.world == 1:
@@ -652,12 +660,27 @@ class ZeroOneAdamW:
                                        count=len(c.owned))
         if advance:
             idx = np.asarray(c.owned, dtype=np.int64)
-            used = grad_ptrs != 0
-            self._steps[idx[used]] += 1  # optimizer.py:181, only tensors that have a gradient
-            steps = np.ascontiguousarray(self._steps[idx])
+            steps = np.ascontiguousarray(self._steps[idx] + (grad_ptrs != 0))
             _lib.call("ha_fill_step_scalars", len(c.owned), _lib.np_ptr(c.lrs), _lib.np_ptr(steps),
                       self.betas[0], self.betas[1], self.weight_decay, _lib.np_ptr(tab))
         c.table.upload()
+
+    def _stage_step(self) -> None:
+        """Uploads the next update's tables ahead of the norm's host read (which leaves the GPU
+        idle until the host launches the update): step() then only launches, if nothing it
+        depends on changed in between (the gradients, the tables, the step counts)."""
+        staged = []
+        for k, c in enumerate(self._classes):
+            grads, ptrs = self._cached_grads(k, c)
+            self._upload_table(c, ptrs, advance=True)
+            staged.append((grads, ptrs))
+        self._staged = (self._table_epoch, self.param_steps.version,
+                        [self.params[i].grad for c in self._classes for i in c.owned], staged,
+                        self._owned_param_ptrs())
+
+    def _owned_param_ptrs(self) -> list[int]:
+        """Addresses of the owned parameters (world 1: the tables point at them directly)."""
+        return [self.params[i].data_ptr() for c in self._classes for i in c.owned] if self.world == 1 else []
 
     # ---------------------------------------------------------------- gradient landing
     def _setup_landing(self) -> None:
@@ -821,6 +844,7 @@ class ZeroOneAdamW:
         self._pending_clip = None
         self._fused_sumsq = None
         self._grad_cache = {}
+        self._staged = None
         self._landed = {}  # what was pushed early no longer matches the gradients
         if self._land_hooks:  # (a backward that raised may have left both behind)
             self._land_pending, self._land_pending_bytes = [], 0
@@ -957,15 +981,18 @@ class ZeroOneAdamW:
                 self._phase("sumsq", False)
             if self.world > 1 and reuse:  # the exchange's square sums, one per class and round
                 self._comm.all_reduce_sum(self._norm_rounds, HA_F64)
+                self._stage_step()
                 partial = self._comm.read(self._norm_rounds, self._norm_rounds_host,
                                           "all-reduce(sum) of the norm").reshape(-1).tolist()
             elif self.world > 1:
                 self._comm.all_reduce_sum(self._norm_buf, HA_F64)
+                self._stage_step()
                 partial = self._comm.read(self._norm_buf, self._norm_host, "all-reduce(sum) of the norm").tolist()
             else:
                 self._norm_host.copy_(self._norm_buf, non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record()
+                self._stage_step()
                 ev.synchronize()
                 partial = self._norm_host.tolist()
         total = np.float32(sum(partial))  # the reference's total is an fp32 tensor
@@ -1012,11 +1039,23 @@ class ZeroOneAdamW:
         with torch.cuda.device(self.device):
             launches, keep = [], []
             updated = np.zeros(len(self.params), dtype=bool)  # tensors this step writes (the used set)
+            staged, self._staged = self._staged, None
+            if staged is not None and (staged[0] != self._table_epoch or staged[1] != self.param_steps.version or
+                                       any(self.params[i].grad is not g for g, i in
+                                           zip(staged[2], (i for c in self._classes for i in c.owned)))):
+                staged = None  # something changed since clip_grad_norm staged the tables
+            if staged is not None and staged[4] != self._owned_param_ptrs():
+                staged = None  # a parameter was re-bound: its table entry must be rewritten
             for k, c in enumerate(self._classes):
-                grads, ptrs = self._cached_grads(k, c)
+                if staged is not None:
+                    grads, ptrs = staged[3][k]
+                else:
+                    grads, ptrs = self._cached_grads(k, c)
+                    self._upload_table(c, ptrs, advance=True)
                 keep.append(grads)
-                self._upload_table(c, ptrs, advance=True)
-                updated[np.asarray(c.owned, dtype=np.int64)[ptrs != 0]] = True
+                idx = np.asarray(c.owned, dtype=np.int64)
+                self._steps[idx[ptrs != 0]] += 1  # optimizer.py:181, only tensors that have a gradient
+                updated[idx[ptrs != 0]] = True
                 sc = _lib.AdamwScalars()
                 _lib.call("ha_make_scalars", self.betas[0], self.betas[1], self.eps, self.weight_decay, c.code,
                           0 if scale is None else 1, 0.0 if scale is None else scale, ctypes.byref(sc))
@@ -1177,6 +1216,7 @@ class ZeroOneAdamW:
                 dst.copy_(src.to(dst.device, torch.float32))
             self._steps[i] = int(state["param_steps"][i])
         self.step_count = int(state["step_count"])
+        self._staged = None
         self._pending_clip = None
         torch.cuda.current_stream(self.device).synchronize()
 

@@ -291,3 +291,50 @@ def test_parameters_written_behind_the_optimizer_are_rewritten():
     for i in range(len(case.shapes)):
         assert_bits_equal(to_numpy(params[i].data, case.dtype), ora.params[i], f"param[{i}]")
         assert_bits_equal(to_numpy(opt.master[i], 0), ora.tensor_state(i)[0], f"master[{i}]")
+
+
+def test_staged_tables_follow_changes_and_skips():
+    """clip_grad_norm uploads the next update's tables before its host read; step() uses them
+    only if nothing changed: a step count edited between the two calls is honoured, and a step
+    the caller skips after clip_grad_norm advances no count."""
+    import torch
+    from helpers import oracle_for
+    case = next(c for c in CASES if c.name == "bf16_clip")
+    params, opt = build(case)
+    ora = oracle_for(case, Z.FORM_TORCH_CUDA)
+
+    def grads_in(s):
+        opt.zero_grad(set_to_none=True)
+        for p, g, shape in zip(params, case.grads(s, 0), case.shapes):
+            p.grad = to_torch(g, case.dtype, shape, "cuda")
+        ora.reduce_grads([case.grads(s, 0)])
+
+    grads_in(0)
+    opt.all_reduce_grads()
+    ora.clip_grad_norm(case.max_norm, norm=opt.clip_grad_norm(case.max_norm))
+    opt.step()
+    ora.step()
+    grads_in(1)  # a count edited between clip_grad_norm and step
+    opt.all_reduce_grads()
+    n = opt.clip_grad_norm(case.max_norm)
+    opt.param_steps[3] = opt.param_steps[3] + 5
+    ora.state[0].param_steps[3] += 5
+    ora.clip_grad_norm(case.max_norm, norm=n)
+    opt.step()
+    ora.step()
+    grads_in(2)  # clip_grad_norm, then the caller skips the step
+    opt.all_reduce_grads()
+    opt.clip_grad_norm(case.max_norm)
+    grads_in(1)
+    opt.all_reduce_grads()
+    ora.clip_grad_norm(case.max_norm, norm=opt.clip_grad_norm(case.max_norm))
+    opt.step()
+    ora.step()
+    torch.cuda.synchronize()
+    for i in range(len(case.shapes)):
+        master, m, v, steps = ora.tensor_state(i)
+        assert opt.param_steps[i] == steps
+        assert_bits_equal(to_numpy(opt.master[i], 0), master, f"master[{i}]")
+        assert_bits_equal(to_numpy(opt.exp_avg[i], 0), m, f"exp_avg[{i}]")
+        assert_bits_equal(to_numpy(opt.exp_avg_sq[i], 0), v, f"exp_avg_sq[{i}]")
+        assert_bits_equal(to_numpy(params[i].data, case.dtype), ora.params[i], f"param[{i}]")
