@@ -23,7 +23,20 @@ import shutil
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
 FILES = ("hybrid_rl/__init__.py", "hybrid_rl/optimizer.py")
-DEFAULT_REFERENCE = os.environ.get("HYBRIDAGENT_REFERENCE", "/root/reference")
+
+
+def _default_reference() -> str:
+    """The reference checkout: $HYBRIDAGENT_REFERENCE, else the path BASELINE.json records."""
+    if os.environ.get("HYBRIDAGENT_REFERENCE"):
+        return os.environ["HYBRIDAGENT_REFERENCE"]
+    try:
+        with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as fh:
+            return json.load(fh)["reference_path"]
+    except (OSError, KeyError, ValueError):
+        return ""
+
+
+DEFAULT_REFERENCE = _default_reference()
 
 
 def sha256(path: str) -> str:
@@ -33,7 +46,7 @@ def sha256(path: str) -> str:
 
 def stage(reference: str = DEFAULT_REFERENCE) -> bool:
     """Stages the files if the checkout exists; returns whether oracle/_ref holds them."""
-    if not all(os.path.exists(os.path.join(reference, f)) for f in FILES):
+    if not reference or not all(os.path.exists(os.path.join(reference, f)) for f in FILES):
         return staged() is not None
     record = {"source": "HybridAgent hybrid_rl (unmodified)", "files": {}}
     for f in FILES:
