@@ -669,7 +669,8 @@ def run_ours(args) -> None:
     peak, peak_kind = measured_hbm_peak()
     adamw_ms = phases.get("adamw")
     # the update reads grad + master/m/v and writes master/m/v (26 B per owned param); the bf16 copy
-    # costs 2 B per param when written in full, else 8 B per changed 4-element group
+    # costs 2 B per param when written in full, else 8 B per stored 4-element group (the groups of
+    # every 32-byte sector that holds a changed value)
     delta = writes["mode"] == "changed groups"
     algo = (26 * owned_params + 8 * writes["changed_groups"]) if delta else ALGO_BYTES_ADAMW["bf16"] * owned_params
     achieved = algo / (adamw_ms * 1e-3) / 1e9 if adamw_ms else None

@@ -107,7 +107,8 @@ __device__ __forceinline__ void push1(const Peers& p, uint64_t local, int64_t k,
 // all-gather's NVLink bytes.
 //
 // `changed` (DELTA, may be null): the number of stored groups (scalar-path elements count as
-// groups) is added to it, one atomic per CTA, so the caller can tell how much moved.
+// groups; on the vector path a changed group stores the three others of its 32-byte sector too)
+// is added to it, one atomic per CTA, so the caller can tell how much moved.
 template <int DT, bool PEERS, bool DELTA>
 __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __restrict__ tensors,
                                                          const ha_chunk* __restrict__ chunks, Scalars s, Peers peers,
@@ -168,7 +169,10 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
       }
 #pragma unroll
       for (int u = 0; u < kGroups; ++u) {
-        if (e[u] + 4 <= end) {
+        const bool full = e[u] + 4 <= end;
+        uint2 w = make_uint2(0, 0);
+        bool changed = false;
+        if (full) {
           uint2 before = make_uint2(0, 0);
           if constexpr (DELTA) before = pack4<DT>(ms[u]);
           adamw_elem(s, decay, neg_lr, rc1, rc2, grad_in<DT>(s, g[u].x), ms[u].x, m[u].x, v[u].x);
@@ -179,16 +183,31 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(const ha_tensor* __rest
           store4_f32(exp_avg, e[u], m[u]);
           store4_f32(exp_avg_sq, e[u], v[u]);
           if constexpr (DT != HA_F32) {
-            const uint2 w = pack4<DT>(ms[u]);
-            if (!DELTA || w.x != before.x || w.y != before.y) {
-              __stcs(reinterpret_cast<uint2*>(static_cast<uint16_t*>(param) + e[u]), w);
-              if constexpr (PEERS) push_raw4(peers, pushed, e[u], w);
-              stored += DELTA;
-            }
+            w = pack4<DT>(ms[u]);
+            changed = w.x != before.x || w.y != before.y;
           } else if constexpr (PEERS) {
             push_f32x4(peers, pushed, e[u], ms[u]);
           }
-        } else {
+        }
+        if constexpr (DT != HA_F32) {
+          // DELTA: the four lanes whose groups share a 32-byte sector store together when any of
+          // them changed (a whole sector, which the memory system writes without fetching it; the
+          // other groups' values are unchanged, so every copy still ends with the same bits).
+          // Every lane of the warp reaches the shuffles: the pass loop is uniform across the CTA.
+          bool store = full;
+          if constexpr (DELTA) {
+            uint32_t any = changed ? 1u : 0u;
+            any |= __shfl_xor_sync(0xffffffffu, any, 1);
+            any |= __shfl_xor_sync(0xffffffffu, any, 2);
+            store = full && any;
+          }
+          if (store) {
+            __stcs(reinterpret_cast<uint2*>(static_cast<uint16_t*>(param) + e[u]), w);
+            if constexpr (PEERS) push_raw4(peers, pushed, e[u], w);
+            stored += DELTA;
+          }
+        }
+        if (!full) {
           for (int64_t k = e[u]; k < end; ++k) one(k);  // ragged tail of the tensor (one thread)
         }
       }

@@ -229,8 +229,9 @@ int ha_adamw_step_peers(const ha_tensor* d_tensors, const ha_chunk* d_chunks, in
  * broadcast of optimizer.py:192-194).  The caller guarantees that on entry every copy of each
  * parameter (local and peers') equals RNE(master); the result is then bit for bit that of a
  * full write on every copy, while unchanged groups cost no HBM write and no NVLink bytes.
- * d_changed_groups (device, may be NULL): the number of groups stored (elements of the scalar
- * paths count one each) is added to it. */
+ * A changed group is stored with the other groups of its 32-byte sector (whole sectors, no
+ * read-modify-write).  d_changed_groups (device, may be NULL): the number of groups stored
+ * (elements of the scalar paths count one each) is added to it. */
 int ha_adamw_step_delta(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks, int64_t chunk_elems,
                         int param_dtype, const ha_adamw_scalars* sc, const ha_peers* peers,
                         unsigned long long* d_changed_groups, void* stream);

@@ -247,9 +247,10 @@ def test_adamw_peer_and_changed_group_stores(code, entry):
     """Parameter stores of the fused update, with two 'peers' emulated on this GPU (arenas at
     fixed offsets from the local parameter arena).  ha_adamw_step_delta: the local parameters
     (and, with peers, every peer) end with the oracle's new values wherever a 4-element group
-    (per element on the scalar path and ragged tails) changed its rounded value; unchanged
-    groups are not stored at all -- a sentinel planted in a peer's copy of an unchanged group
-    survives, one in a changed group is overwritten.  ha_adamw_step_peers stores every group."""
+    (per element on the scalar path and ragged tails) changed its rounded value, the other groups
+    of its 32-byte sector with it; groups in unchanged sectors are not stored at all -- a sentinel
+    planted in a peer's copy there survives, one in a changed sector is overwritten.
+    ha_adamw_step_peers stores every group."""
     import torch
     sizes = SIZES + [3 * 16384 + 6]
     n = len(sizes)
@@ -313,10 +314,15 @@ def test_adamw_peer_and_changed_group_stores(code, entry):
         if entry == "dense_peers":
             stored[:] = ts.np_grad[k] is not None
         elif ts.np_grad[k] is not None and k not in (4, 13):
+            # vector path: 4-element groups; the four groups of a 32-byte sector (16 elements) are
+            # stored together when any of them changed
             full = size // 4 * 4
             grp = diff[:full].reshape(-1, 4).any(axis=1)
-            stored[:full] = np.repeat(grp, 4)
-            want_count += int(grp.sum()) + int(diff[full:].sum())
+            quad = np.zeros(-(-len(grp) // 4) * 4, dtype=bool)
+            quad[:len(grp)] = grp
+            quad = np.repeat(quad.reshape(-1, 4).any(axis=1), 4)[:len(grp)]
+            stored[:full] = np.repeat(quad, 4)
+            want_count += int(quad.sum()) + int(diff[full:].sum())
         elif ts.np_grad[k] is not None:
             want_count += int(diff.sum())  # scalar path: one per changed element
         if entry == "delta_local":
