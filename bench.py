@@ -17,13 +17,22 @@ Printed (rank 0, one JSON line):
                pinned host memory each step (H2D inside the timed region, on a copy
                stream into a second gradient set so that step k+1's copy overlaps step
                k's optimizer) and the norm read back (D2H);
-  roofline     the fused AdamW kernel: 28 algorithmic bytes per owned parameter over its
-               CUDA-event duration on the launch stream, against the measured HBM copy
-               peak; traffic = ncu DRAM bytes per launch from the committed profile;
-  cpu_baseline the reference's op sequence on this host's CPU cores (N=1, rank 0), on a
-               bounded sample of the same parameter set;
+  roofline     N=1: the fused AdamW kernel's algorithmic bytes (26 B per owned parameter plus
+               the stored bf16 groups, or 28 B with full writes) over its CUDA-event
+               duration on the launch stream, against the measured HBM copy peak; traffic =
+               ncu DRAM bytes per parameter from the committed record of that write mode.
+               N>1: the longest phase (push or update + all-gather) with the resource that
+               binds it, NVLink against the probed link peak (profiles/nvlink_peak.json)
+               and the nominal 900 GB/s; every phase in ``roofline_fused``;
+  parity       one more step after timing, checked at ~100,000 seeded positions per rank
+               against torch's CUDA kernels running the reference's op sequence;
+  cpu_baseline the reference's own optimizer (staged unmodified by oracle/stage_ref.py) on
+               this host's CPU cores (N=1, rank 0), on a bounded sample of the same
+               parameter set (configuration 1: the whole of it);
   clocks       nvidia-smi samples taken during the timed region.
-``--impl reference`` times only that CPU implementation (rank 0; other ranks exit).
+``--impl reference`` times only that CPU implementation (rank 0; other ranks exit), for the
+steps and warm-up it prints, plus BASELINE configuration 1 whole (``config1``).
+``--probe-links`` (N > 1) measures NVLink bandwidth between the GPUs instead.
 
 ``--landing`` (N > 1) measures gradient landing instead and prints its own JSON line: a
 synthetic forward + backward whose weight gradients are GEMMs over ``--tokens`` tokens
@@ -477,6 +486,20 @@ def profiled_traffic_per_param(mode: str) -> tuple[float | None, str | None]:
         return None, None
 
 
+def phase_roofline(how: str, ms: float, hbm_bytes: float, link_bytes: float, hbm_peak: float,
+                   link_peak: float) -> dict:
+    """One phase of a multi-GPU step against both of its resources: the target time is the
+    slower of its HBM bytes at the HBM peak and its NVLink bytes at the link peak (GB/s), the
+    resource that sets it is the bound, and ``frac`` = target / measured."""
+    t_hbm, t_link = hbm_bytes / (hbm_peak * 1e9), link_bytes / (link_peak * 1e9)
+    gbs = link_bytes / (ms * 1e-3) / 1e9
+    return {"how": how, "bound": "nvlink" if t_link >= t_hbm else "hbm", "measured_ms": round(ms, 3),
+            "target_ms": round(max(t_hbm, t_link) * 1e3, 3), "frac": round(max(t_hbm, t_link) * 1e3 / ms, 4),
+            "nvlink_bytes": int(link_bytes), "hbm_bytes": int(hbm_bytes), "link_gbs_achieved": round(gbs, 1),
+            "hbm_gbs_achieved": round(hbm_bytes / (ms * 1e-3) / 1e9, 1), "frac_of_link_peak": round(gbs / link_peak, 4),
+            "frac_of_nominal_link": round(gbs / NOMINAL_NVLINK_GBS, 4)}
+
+
 def measured_link_peak(world: int) -> tuple[float, str]:
     """Per-direction NVLink bandwidth at this world size: the best pattern of the committed
     ``bench.py --probe-links`` record at that size (or the nearest size probed), else the
@@ -692,10 +715,9 @@ def run_ours(args) -> None:
         # per phase: its HBM bytes and the bytes it moves over NVLink per GPU; the phase is bound by
         # whichever takes longer at its measured peak, and the roofline line names the longest
         # phase with that resource.  push: this rank's gradients of the other ranks' tensors
-        # ((W-1)/W of 2 B/param).  adamw: the update (28 B per owned param in HBM) and the
-        # parameter all-gather: 2 B x (W-1) per owned param with the copy engines, or -- the
-        # fused update -- only the 4-element groups whose bf16 value changed (the changed fraction
-        # is the checked step's, sampled; groups ~ 1-(1-p)^4 of them)
+        # ((W-1)/W of 2 B/param).  adamw: the update (its algorithmic HBM bytes, `algo`) and the
+        # parameter all-gather: 2 B x (W-1) per owned param with full writes, or only the stored
+        # groups (the update kernel's own count) with changed-sector writes
         link, link_src = measured_link_peak(world)
         foreign = n_params - owned_params
         push_how = ("copy engines, one stream per peer" if opt.push_streams < 0 else
@@ -717,18 +739,8 @@ def run_ours(args) -> None:
         for name, how, link_bytes, hbm_bytes in (("push", push_how, 2 * foreign, 4 * n_params),
                                                  ("adamw", gather_how, adamw_link, algo + int(2 * foreign * moved))):
             ms_phase = phases.get(name)
-            if not ms_phase:
-                continue
-            t_hbm, t_link = hbm_bytes / (peak * 1e9), link_bytes / (link * 1e9)
-            bound = "nvlink" if t_link >= t_hbm else "hbm"
-            gbs = link_bytes / (ms_phase * 1e-3) / 1e9
-            nvlink[name] = {"how": how, "bound": bound, "measured_ms": round(ms_phase, 3),
-                            "target_ms": round(max(t_hbm, t_link) * 1e3, 3),
-                            "frac": round(max(t_hbm, t_link) * 1e3 / ms_phase, 4), "nvlink_bytes": link_bytes,
-                            "hbm_bytes": hbm_bytes, "link_gbs_achieved": round(gbs, 1),
-                            "hbm_gbs_achieved": round(hbm_bytes / (ms_phase * 1e-3) / 1e9, 1),
-                            "frac_of_link_peak": round(gbs / link, 4),
-                            "frac_of_nominal_link": round(gbs / NOMINAL_NVLINK_GBS, 4)}
+            if ms_phase:
+                nvlink[name] = phase_roofline(how, ms_phase, hbm_bytes, link_bytes, peak, link)
         dom = max((k for k in ("push", "adamw") if k in nvlink), key=lambda k: nvlink[k]["measured_ms"], default=None)
         if dom is not None and nvlink[dom]["bound"] == "nvlink":
             d = nvlink[dom]

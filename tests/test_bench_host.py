@@ -49,3 +49,13 @@ def test_sampled_positions_cover_every_tensor_edge():
         got.update(base + int(x) for x in idx)
     assert starts <= got and {4, 5, 70005, 70008} <= got
     assert sp.k == len(got)
+
+
+def test_phase_roofline_names_the_binding_resource():
+    # the W=8 push of the Qwen3-8B set: 14.33 GB over NVLink, 32.8 GB in HBM, 20.53 ms
+    push = bench.phase_roofline("push", 20.53, 4 * 8_190_735_360, 2 * 7_166_893_440, 6554.9, 705.7)
+    assert push["bound"] == "nvlink" and abs(push["link_gbs_achieved"] - 698.2) < 1.0
+    assert abs(push["frac"] - push["frac_of_link_peak"]) < 1e-3
+    # its update: 26.6 GB in HBM, 83 MB of changed sectors to the peers, 5.0 ms
+    upd = bench.phase_roofline("adamw", 5.006, 26.6e9, 82.5e6, 6554.9, 705.7)
+    assert upd["bound"] == "hbm" and abs(upd["frac"] - 26.6e9 / 6554.9e9 / 5.006e-3) < 1e-3
