@@ -57,7 +57,7 @@ def test_exchange_pieces_write_every_summed_element_once_per_round(numels, world
 
 
 @settings(max_examples=100, deadline=None)
-@given(sizes_st, st.integers(min_value=2, max_value=9), rounds_st, st.integers(min_value=0, max_value=4),
+@given(sizes_st, st.integers(min_value=2, max_value=9), rounds_st, st.integers(min_value=-1, max_value=4),
        st.floats(min_value=0.0, max_value=1.0))
 def test_round_push_split_and_landing_pieces_partition(numels, world, units, streams, share):
     p = layout.plan(numels, [HA_BF16] * len(numels), world)
@@ -65,10 +65,14 @@ def test_round_push_split_and_landing_pieces_partition(numels, world, units, str
     pc = layout.exchange_pieces(cls, p.owner, numels, units * layout.ALIGN)
     for rank in range(world):
         for k in range(pc.n_rounds):
-            kernel, groups = layout.round_push_split(pc, k, rank, streams, share)
+            kernel, groups = layout.round_push_split(pc, k, rank, streams, share, world)
             ce = np.concatenate(groups) if groups else np.zeros(0, np.int64)
             assert sorted(kernel.tolist() + ce.tolist()) == np.nonzero(pc.round == k)[0].tolist()
             assert (pc.owner[ce] != rank).all()
+            if streams < 0:  # one group per destination, in rotation from rank + 1
+                assert len(groups) == world - 1
+                for j, g in enumerate(groups):
+                    assert (pc.owner[g] == (rank + 1 + j) % world).all()
     lp = layout.landing_pieces(pc, len(cls.indices))
     flat = np.concatenate(lp) if lp else np.zeros(0, np.int64)
     assert sorted(flat.tolist()) == np.nonzero((pc.round < layout.LAND_ROUNDS) & (pc.tensor >= 0))[0].tolist()
@@ -86,3 +90,24 @@ def test_balanced_groups_are_a_partition_within_one_item(sizes, n):
     if sizes:
         loads = [sum(sizes[int(e) - 100] for e in g) for g in groups]
         assert max(loads) - min(loads) <= max(sizes)
+
+
+@settings(max_examples=150, deadline=None)
+@given(sizes_st, world_st, st.integers(min_value=1, max_value=200_000))
+def test_gather_parts_cover_each_owned_segment(numels, world, part):
+    """The copy-engine all-gather's parts: consecutive chunk ranges in segment order, each
+    part's element range holding all of its chunks and the parts' ranges never overlapping."""
+    p = layout.plan(numels, [HA_BF16] * len(numels), world)
+    (cls,) = p.classes
+    for r in range(world):
+        owned = cls.owned(p.owner, r)
+        if not owned:
+            continue
+        own_numels = [numels[i] for i in owned]
+        chunks = layout.chunk_table(own_numels, 16384)
+        parts = layout.gather_parts(chunks, [cls.offset[i] for i in owned], own_numels, 16384, part)
+        assert parts[0][0] == 0 and sum(q[1] for q in parts) == len(chunks)
+        for (c0, nc, e0, e1), nxt in zip(parts, parts[1:] + [None]):
+            assert 0 < nc and e0 < e1 <= cls.own_len[r]
+            if nxt is not None:
+                assert nxt[0] == c0 + nc and nxt[2] >= e1
