@@ -34,12 +34,13 @@ Printed (rank 0, one JSON line):
 steps and warm-up it prints, plus BASELINE configuration 1 whole (``config1``).
 ``--probe-links`` (N > 1) measures NVLink bandwidth between the GPUs instead.
 
-``--landing`` (N > 1) measures gradient landing instead and prints its own JSON line: a
-synthetic forward + backward whose weight gradients are GEMMs over ``--tokens`` tokens
-(one ``linear`` per matrix, a dot product per vector) followed by the optimizer sequence,
-with the early pushes off and on (same optimizer, receive window sized for two rounds so
-the whole exchange can start during backward); per variant the forward + backward time,
-the optimizer time left after backward, and their sum, max over ranks.
+``--landing`` measures gradient landing instead and prints its own JSON line: a synthetic
+forward + backward whose weight gradients are GEMMs over ``--tokens`` tokens (one ``linear``
+per matrix, a dot product per vector) followed by the optimizer sequence, with landing off and
+on (same optimizer).  N > 1: the early pushes of the exchange, receive window sized for two
+rounds so the whole exchange can start during backward; N = 1: the norm's square sums taken as
+the gradients land.  Per variant the forward + backward time, the optimizer time left after
+backward, and their sum, max over ranks.
 """
 from __future__ import annotations
 
@@ -82,14 +83,14 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-params", type=int, default=200_000_000)
     ap.add_argument("--max-params", type=int, default=0, help="truncate the parameter set (smoke / profiling)")
-    ap.add_argument("--landing", action="store_true", help="measure gradient landing (N > 1)")
+    ap.add_argument("--landing", action="store_true", help="measure gradient landing")
     ap.add_argument("--tokens", type=int, default=2048, help="tokens of the --landing synthetic backward")
     ap.add_argument("--probe-links", action="store_true", help="measure NVLink bandwidth between the N GPUs")
     ap.add_argument("--probe-bytes", type=int, default=2 << 30, help="--probe-links: bytes each rank moves")
     ap.add_argument("--parity-per-rank", type=int, default=100_000,
                     help="sampled positions per rank of the checked step after timing (0: no check)")
-    ap.add_argument("--land-ctas", default="0,64", help="--landing: comma-separated CTA caps of the early "
-                    "pushes to measure (0: copy engines)")
+    ap.add_argument("--land-ctas", default="0,64", help="--landing: comma-separated CTA caps to measure, of "
+                    "the early pushes at N > 1 (0: copy engines), of the square sums at N = 1 (0: one per chunk)")
     return ap.parse_args()
 
 
@@ -791,7 +792,8 @@ def run_ours(args) -> None:
 
 
 def run_landing(args) -> None:
-    """Gradient landing: forward + backward + optimizer step, early pushes off vs on."""
+    """Gradient landing: forward + backward + optimizer step, landing off vs on (N > 1: the early
+    pushes of the exchange; N = 1: the norm's square sums taken as the gradients land)."""
     import torch
     import torch.distributed as dist
     import torch.nn.functional as F
@@ -801,17 +803,19 @@ def run_landing(args) -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus or world < 2:
-        raise SystemExit("--landing needs --gpus N > 1 under torchrun")
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     shapes = workloads.WORKLOADS[args.workload]()
     if args.max_params:
         shapes = workloads.truncated(shapes, args.max_params)
     n_params = sum(math.prod(s) for s in shapes)
     # a receive window of two rounds: every piece may be pushed while its gradient lands
-    os.environ["HYBRIDAGENT_B200_RECV_BYTES"] = str(2 * n_params + (256 << 20))
+    if world > 1:
+        os.environ["HYBRIDAGENT_B200_RECV_BYTES"] = str(2 * n_params + (256 << 20))
     gen = torch.Generator(device=dev).manual_seed(1234)
     params = [torch.nn.Parameter((torch.randn(s, device=dev, generator=gen) * 0.02).to(torch.bfloat16))
               for s in shapes]
@@ -849,13 +853,14 @@ def run_landing(args) -> None:
     caps = [int(x) for x in args.land_ctas.split(",")]
     for variant in ["off"] + [f"on_ctas{n}" for n in caps]:
         opt.landing_enabled = variant != "off"
-        if opt.landing_enabled:
+        if opt.landing_enabled:  # N > 1: CTAs of the early pushes; N = 1: of the square sums
             opt.land_ctas = int(variant[len("on_ctas"):])
-        launches0 = opt.land_launches
+        launches0 = opt.land_launches if world > 1 else opt.land_norm_steps
         evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
         for _ in range(max(args.warmup, 3)):
             one([torch.cuda.Event(enable_timing=True) for _ in range(3)])
-        dist.barrier()
+        if world > 1:
+            dist.barrier()
         torch.cuda.synchronize()
         for ev in evs:
             one(ev)
@@ -863,24 +868,31 @@ def run_landing(args) -> None:
         fb = sum(e[0].elapsed_time(e[1]) for e in evs) / len(evs)
         st = sum(e[1].elapsed_time(e[2]) for e in evs) / len(evs)
         t = torch.tensor([fb, st, fb + st], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
         out[variant] = {"fwd_bwd_ms": round(float(t[0]), 3), "step_after_backward_ms": round(float(t[1]), 3),
-                        "total_ms": round(float(t[2]), 3),
-                        "early_push_calls_per_step": (opt.land_launches - launches0) // (len(evs) + max(args.warmup, 3))}
+                        "total_ms": round(float(t[2]), 3)}
+        n_steps = len(evs) + max(args.warmup, 3)
+        if world > 1:
+            out[variant]["early_push_calls_per_step"] = (opt.land_launches - launches0) // n_steps
+        else:
+            out[variant]["landed_norm_steps"] = f"{opt.land_norm_steps - launches0}/{n_steps}"
     best = min((k for k in out if k != "off"), key=lambda k: out[k]["total_ms"])
     if rank == 0:
         line = {"metric": "fwd_bwd_plus_step_ms", "value": out[best]["total_ms"], "unit": "ms", "n_gpus": world,
                 "steps": args.steps, "warmup": max(args.warmup, 3), "higher_is_better": False, "scaling": "strong",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": args.workload, "params": n_params, "tensors": len(shapes), "tokens": T,
-                           "recv_window_bytes": int(os.environ["HYBRIDAGENT_B200_RECV_BYTES"]),
+                           "recv_window_bytes": int(os.environ["HYBRIDAGENT_B200_RECV_BYTES"]) if world > 1 else 0,
                            "comm_mode": opt.comm_mode, "parallelism": f"zero1-dp{world}"},
                 "landing": out, "best": best,
                 "saved_ms": round(out["off"]["total_ms"] - out[best]["total_ms"], 3)}
         print(json.dumps(line), flush=True)
-    dist.barrier()
+    if world > 1:
+        dist.barrier()
     opt.close()
-    dist.destroy_process_group()
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def run_probe_links(args) -> None:

@@ -63,6 +63,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "ha_adamw_step": ([_vp, _vp, _i64, _i64, ctypes.c_int, ctypes.c_int, ctypes.POINTER(AdamwScalars), _vp],
                       ctypes.c_int),
     "ha_grad_sumsq": ([_vp, _vp, _i64, _i64, ctypes.c_int, _vp, _vp, _vp], ctypes.c_int),
+    "ha_grad_sumsq_ctas": ([_vp, _vp, _i64, _i64, ctypes.c_int, _vp, _vp, ctypes.c_int, _vp], ctypes.c_int),
     "ha_grad_sumsq_noalloc": ([_vp, _vp, _i64, _i64, ctypes.c_int, _vp, _vp], ctypes.c_int),
     "ha_scale_grads": ([_vp, _vp, _i64, _i64, ctypes.c_int, _f32, _vp], ctypes.c_int),
     "ha_gather": ([_vp, _vp, _i64, _i64, ctypes.c_int, _vp], ctypes.c_int),

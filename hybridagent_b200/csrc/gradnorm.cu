@@ -77,43 +77,54 @@ __device__ __forceinline__ double block_sum(double x, double* smem) {
   return x;  // valid in thread 0
 }
 
+// One CTA per chunk, or fewer CTAs each taking chunks blockIdx.x, blockIdx.x + gridDim.x, ...
+// (a capped grid leaves SMs to kernels running beside it).  Either way every chunk writes its
+// own partial, computed the same way, so the result does not depend on the grid.
 template <int DT>
 __global__ void __launch_bounds__(kThreads) sumsq_kernel(const ha_tensor* __restrict__ tensors,
-                                                         const ha_chunk* __restrict__ chunks,
+                                                         const ha_chunk* __restrict__ chunks, int64_t n_chunks,
                                                          double* __restrict__ partials) {
   __shared__ StagedChunk sc;
   __shared__ double red[kThreads / 32];
-  stage_chunk(tensors, chunks, &sc);
-  double acc = 0.0;
-  if (sc.t.grad != 0) {
-    constexpr int V = Vec<DT>::n;
-    using raw = typename Elem<DT>::raw;
-    const raw* grad = reinterpret_cast<const raw*>(sc.t.grad);
-    const int64_t begin = int64_t(sc.index) * kChunk;
-    const int64_t end = min(begin + kChunk, sc.t.numel);
-    if ((sc.t.grad & 15) == 0) {
-      constexpr int kPerPass = kThreads * V;       // elements per CTA pass
-      constexpr int kUnroll = 4;                   // loads in flight per thread
-      int64_t e = begin + int64_t(threadIdx.x) * V;
-      for (; e + int64_t(kUnroll - 1) * kPerPass + V <= end; e += int64_t(kUnroll) * kPerPass) {
-        uint4 w[kUnroll];
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) w[u] = __ldcs(reinterpret_cast<const uint4*>(grad + e + u * kPerPass));
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) acc += double(vec_sumsq<DT>(w[u]));
-      }
-      for (; e + V <= end; e += kPerPass) acc += double(vec_sumsq<DT>(__ldcs(reinterpret_cast<const uint4*>(grad + e))));
-      if (e < end) {  // ragged tail of the tensor: at most V-1 elements, one thread
-        float s = 0.0f;
-        for (int64_t k = e; k < end; ++k) s = __fadd_rn(s, sq<DT>(Elem<DT>::widen(grad[k])));
-        acc += double(s);
-      }
-    } else {
-      for (int64_t k = begin + threadIdx.x; k < end; k += kThreads) acc += double(sq<DT>(Elem<DT>::widen(grad[k])));
+  for (int64_t ci = blockIdx.x; ci < n_chunks; ci += gridDim.x) {
+    if (threadIdx.x < 4) {
+      const ha_chunk c = chunks[ci];
+      reinterpret_cast<uint4*>(&sc.t)[threadIdx.x] = reinterpret_cast<const uint4*>(tensors + c.tensor)[threadIdx.x];
+      if (threadIdx.x == 0) sc.index = c.index;
     }
+    __syncthreads();
+    double acc = 0.0;
+    if (sc.t.grad != 0) {
+      constexpr int V = Vec<DT>::n;
+      using raw = typename Elem<DT>::raw;
+      const raw* grad = reinterpret_cast<const raw*>(sc.t.grad);
+      const int64_t begin = int64_t(sc.index) * kChunk;
+      const int64_t end = min(begin + kChunk, sc.t.numel);
+      if ((sc.t.grad & 15) == 0) {
+        constexpr int kPerPass = kThreads * V;       // elements per CTA pass
+        constexpr int kUnroll = 4;                   // loads in flight per thread
+        int64_t e = begin + int64_t(threadIdx.x) * V;
+        for (; e + int64_t(kUnroll - 1) * kPerPass + V <= end; e += int64_t(kUnroll) * kPerPass) {
+          uint4 w[kUnroll];
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) w[u] = __ldcs(reinterpret_cast<const uint4*>(grad + e + u * kPerPass));
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) acc += double(vec_sumsq<DT>(w[u]));
+        }
+        for (; e + V <= end; e += kPerPass) acc += double(vec_sumsq<DT>(__ldcs(reinterpret_cast<const uint4*>(grad + e))));
+        if (e < end) {  // ragged tail of the tensor: at most V-1 elements, one thread
+          float s = 0.0f;
+          for (int64_t k = e; k < end; ++k) s = __fadd_rn(s, sq<DT>(Elem<DT>::widen(grad[k])));
+          acc += double(s);
+        }
+      } else {
+        for (int64_t k = begin + threadIdx.x; k < end; k += kThreads) acc += double(sq<DT>(Elem<DT>::widen(grad[k])));
+      }
+    }
+    acc = block_sum(acc, red);
+    if (threadIdx.x == 0) partials[ci] = acc;
+    __syncthreads();  // sc and red are rewritten for the next chunk
   }
-  acc = block_sum(acc, red);
-  if (threadIdx.x == 0) partials[blockIdx.x] = acc;
 }
 
 // One CTA adds the per-chunk partials: thread i takes partials i, i+1024, ... in order
@@ -140,9 +151,16 @@ __global__ void __launch_bounds__(kFinalThreads) finalize_kernel(const double* _
 
 extern "C" int ha_grad_sumsq(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,
                              int64_t chunk_elems, int grad_dtype, double* d_partials, double* d_out, void* stream) {
+  return ha_grad_sumsq_ctas(d_tensors, d_chunks, n_chunks, chunk_elems, grad_dtype, d_partials, d_out, 0, stream);
+}
+
+extern "C" int ha_grad_sumsq_ctas(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks,
+                                  int64_t chunk_elems, int grad_dtype, double* d_partials, double* d_out,
+                                  int max_ctas, void* stream) {
   HA_NVTX_RANGE();
   using namespace ha;
   if (chunk_elems != HA_SUMSQ_CHUNK) return fail(HA_ERR_INVALID, "ha_grad_sumsq: chunk_elems must be %d", HA_SUMSQ_CHUNK);
+  if (max_ctas < 0) return fail(HA_ERR_INVALID, "ha_grad_sumsq_ctas: max_ctas %d", max_ctas);
   if (!valid_float_dtype(grad_dtype)) return fail(HA_ERR_UNSUPPORTED, "ha_grad_sumsq: grad dtype %d", grad_dtype);
   if (n_chunks < 0 || n_chunks > 0x7fffffffLL) return fail(HA_ERR_INVALID, "ha_grad_sumsq: n_chunks %lld", (long long)n_chunks);
   if (d_out == nullptr) return fail(HA_ERR_INVALID, "ha_grad_sumsq: NULL output");
@@ -150,11 +168,11 @@ extern "C" int ha_grad_sumsq(const ha_tensor* d_tensors, const ha_chunk* d_chunk
     return fail(HA_ERR_INVALID, "ha_grad_sumsq: NULL table or partials");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (n_chunks > 0) {
-    const dim3 grid(static_cast<unsigned>(n_chunks));
+    const dim3 grid(static_cast<unsigned>(max_ctas > 0 && max_ctas < n_chunks ? max_ctas : n_chunks));
     switch (grad_dtype) {
-      case HA_F32: sumsq_kernel<HA_F32><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, d_partials); break;
-      case HA_BF16: sumsq_kernel<HA_BF16><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, d_partials); break;
-      default: sumsq_kernel<HA_F16><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, d_partials); break;
+      case HA_F32: sumsq_kernel<HA_F32><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, n_chunks, d_partials); break;
+      case HA_BF16: sumsq_kernel<HA_BF16><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, n_chunks, d_partials); break;
+      default: sumsq_kernel<HA_F16><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, n_chunks, d_partials); break;
     }
     const int rc = check_launch("sumsq_kernel");
     if (rc != HA_OK) return rc;
@@ -262,9 +280,9 @@ extern "C" int ha_grad_sumsq_noalloc(const ha_tensor* d_tensors, const ha_chunk*
   if (n_chunks > 0) {
     const dim3 grid(static_cast<unsigned>(n_chunks));
     switch (grad_dtype) {
-      case HA_F32: sumsq_kernel<HA_F32><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, partials); break;
-      case HA_BF16: sumsq_kernel<HA_BF16><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, partials); break;
-      default: sumsq_kernel<HA_F16><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, partials); break;
+      case HA_F32: sumsq_kernel<HA_F32><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, n_chunks, partials); break;
+      case HA_BF16: sumsq_kernel<HA_BF16><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, n_chunks, partials); break;
+      default: sumsq_kernel<HA_F16><<<grid, kThreads, 0, st>>>(d_tensors, d_chunks, n_chunks, partials); break;
     }
     const int rc = check_launch("sumsq_kernel (noalloc)");
     if (rc != HA_OK) return rc;

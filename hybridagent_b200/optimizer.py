@@ -427,8 +427,12 @@ class ZeroOneAdamW:
         self.land_launches = 0  # early pushes launched from the landing hooks
         self._land_hooks: list = []
         self._landed: dict[int, tuple[torch.Tensor, int]] = {}  # index -> (gradient, its version when pushed)
+        self._lland = False  # world 1: square sums taken as gradients land (_setup_landing_local)
+        self.land_norm_steps = 0  # clip_grad_norm calls served by those sums
         if land_grads and self.comm_mode == "p2p":
             self._setup_landing()
+        elif land_grads and self.world == 1:
+            self._setup_landing_local()
 
     def _setup_world(self) -> None:
         """Owners' parameter values to every rank (the reference's broadcast), then the
@@ -838,6 +842,136 @@ class ZeroOneAdamW:
         self._land_callback = False
         torch.cuda.current_stream(self.device).wait_stream(self._land_stream)
 
+    # ---------------------------------------------------------------- gradient landing, world size 1
+    def _setup_landing_local(self) -> None:
+        """Gradient landing at world size 1: the norm's square sums are taken while backward is
+        still running.  A post-accumulate-grad hook on every parameter (train.py:268's
+        ``loss.backward()`` hands each gradient over there) queues the gradient; every
+        HYBRIDAGENT_B200_LAND_BUCKET_BYTES and at the end of each backward pass the queued
+        gradients' sums of squares are launched on a side stream (one ``ha_grad_sumsq_ctas`` per
+        dtype class, each into its own fp64 slot, on at most ``land_ctas`` CTAs -- 0: one per
+        chunk -- so that backward keeps the other SMs).  ``clip_grad_norm`` then adds the slots instead of
+        reading every gradient again -- if every owned gradient landed exactly once and is the
+        same object, unmodified (torch's version counter), that it is now; otherwise it takes the
+        full pass.  Results are the same sums of the same squares, grouped per landing."""
+        self._lland = True
+        self._lland_stream = torch.cuda.Stream(device=self.device)
+        self._lland_bucket = int(os.environ.get("HYBRIDAGENT_B200_LAND_BUCKET_BYTES", str(256 << 20)))
+        self.land_ctas = int(os.environ.get("HYBRIDAGENT_B200_LAND_CTAS", "0"))
+        n_chunks = sum(c.sumsq_chunks[1] for c in self._classes)
+        self._lland_cap = (max(2 * len(self.params), 1), max(2 * n_chunks, 1))  # tensors, chunks (two landings each)
+        csz, tsz = _lib.CHUNK_DTYPE.itemsize, _lib.TENSOR_DTYPE.itemsize
+        dev = self.device
+        self._lland_tab = (torch.empty(self._lland_cap[0] * tsz, dtype=torch.uint8, pin_memory=True),
+                           torch.empty(self._lland_cap[0] * tsz, dtype=torch.uint8, device=dev))
+        self._lland_chk = (torch.empty(self._lland_cap[1] * csz, dtype=torch.uint8, pin_memory=True),
+                           torch.empty(self._lland_cap[1] * csz, dtype=torch.uint8, device=dev))
+        self._lland_partials = torch.empty(self._lland_cap[1], dtype=torch.float64, device=dev)
+        self._lland_out = torch.zeros(self._lland_cap[0], dtype=torch.float64, device=dev)
+        self._lland_out_host = torch.zeros(self._lland_cap[0], dtype=torch.float64, pin_memory=True)
+        self._lland_class_of = {i: ci for ci, c in enumerate(self._classes) for i in c.owned}
+        self._lland_reset()
+        me = weakref.ref(self)
+
+        def hook(i):
+            def on_landed(p):
+                opt = me()
+                if opt is not None and opt.landing_enabled:
+                    opt._lland_on_landed(i, p)
+            return on_landed
+
+        self._land_hooks = [p.register_post_accumulate_grad_hook(hook(i)) for i, p in enumerate(self.params)]
+        self.landing_enabled = True
+
+    def _lland_reset(self) -> None:
+        self._lland_pending: list = []  # (parameter index, gradient, stream it was accumulated on)
+        self._lland_bytes = 0
+        self._lland_seen: dict[int, tuple] = {}  # parameter index -> (gradient, its version when summed)
+        self._lland_slots = 0     # fp64 slots written so far this step
+        self._lland_cursor = [0, 0]  # table entries, chunks used in the arenas
+        self._lland_valid = True  # no gradient summed twice, nothing out of room, no in-place clip
+        self._lland_callback = False
+
+    def _lland_on_landed(self, i: int, p: torch.Tensor) -> None:
+        g = p.grad
+        if g is None or i not in self._lland_class_of or not g.is_contiguous():
+            self._lland_valid = False
+            return
+        self._lland_pending.append((i, g, torch.cuda.current_stream(self.device)))
+        self._lland_bytes += g.numel() * g.element_size()
+        if not self._lland_callback:
+            self._lland_callback = True
+            torch.autograd.Variable._execution_engine.queue_callback(self._lland_end_of_backward)
+        if self._lland_bytes >= self._lland_bucket:
+            self._lland_flush()
+
+    def _lland_end_of_backward(self) -> None:
+        self._lland_callback = False
+        self._lland_flush()
+
+    def _lland_flush(self) -> None:
+        """Launches the sums of squares of the queued gradients on the landing stream."""
+        pending, self._lland_pending, self._lland_bytes = self._lland_pending, [], 0
+        if not pending:
+            return
+        land = self._lland_stream
+        csz, tsz = _lib.CHUNK_DTYPE.itemsize, _lib.TENSOR_DTYPE.itemsize
+        with torch.cuda.device(self.device):
+            for st in {st.cuda_stream: st for *_, st in pending}.values():
+                land.wait_stream(st)  # the gradients are complete
+            by_class: dict[int, list] = {}
+            for i, g, _ in pending:
+                if i in self._lland_seen:
+                    self._lland_valid = False  # landed again: its earlier sum is stale
+                by_class.setdefault(self._lland_class_of[i], []).append((i, g))
+            for ci, items in by_class.items():
+                c = self._classes[ci]
+                numels = [g.numel() for _, g in items]
+                chunks = layout.chunk_table(numels, HA_SUMSQ_CHUNK)
+                t0, k0 = self._lland_cursor
+                if (t0 + len(items) > self._lland_cap[0] or k0 + len(chunks) > self._lland_cap[1]
+                        or self._lland_slots >= self._lland_cap[0]):
+                    self._lland_valid = False  # out of room: clip_grad_norm takes the full pass
+                    continue
+                tab = np.zeros(len(items), dtype=_lib.TENSOR_DTYPE)
+                tab["grad"] = [g.data_ptr() for _, g in items]
+                tab["numel"] = numels
+                ht, dt = self._lland_tab
+                hk, dk = self._lland_chk
+                ht.numpy()[t0 * tsz:(t0 + len(items)) * tsz] = tab.view(np.uint8)
+                hk.numpy()[k0 * csz:(k0 + len(chunks)) * csz] = chunks.view(np.uint8)
+                with torch.cuda.stream(land):
+                    dt[t0 * tsz:(t0 + len(items)) * tsz].copy_(ht[t0 * tsz:(t0 + len(items)) * tsz], non_blocking=True)
+                    dk[k0 * csz:(k0 + len(chunks)) * csz].copy_(hk[k0 * csz:(k0 + len(chunks)) * csz], non_blocking=True)
+                slot = self._lland_slots
+                _lib.call("ha_grad_sumsq_ctas", dt.data_ptr() + t0 * tsz, dk.data_ptr() + k0 * csz, len(chunks),
+                          HA_SUMSQ_CHUNK, c.code, self._lland_partials.data_ptr() + k0 * 8,
+                          self._lland_out.data_ptr() + slot * 8, self.land_ctas, land.cuda_stream)
+                self.launches += 2 if len(chunks) else 1
+                self._lland_slots += 1
+                self._lland_cursor = [t0 + len(items), k0 + len(chunks)]
+                for i, g in items:
+                    self._lland_seen[i] = (g, g._version)
+            for _, g, _ in pending:
+                g.record_stream(land)  # the allocator keeps it until its sum has read it
+
+    def _lland_ready(self) -> bool:
+        """Every owned gradient present now landed once, unchanged since; none landed that is
+        gone."""
+        if not (self._lland and self._lland_valid and self._lland_slots):
+            return False
+        present = 0
+        for c in self._classes:
+            for i in c.owned:
+                g = self.params[i].grad
+                if g is None:
+                    continue
+                present += 1
+                seen = self._lland_seen.get(i)
+                if seen is None or seen[0] is not g or seen[1] != g._version:
+                    return False
+        return present == len(self._lland_seen)
+
     # ---------------------------------------------------------------- reference surface
     def zero_grad(self, set_to_none: bool = True) -> None:
         """optimizer.py:88-93."""
@@ -846,7 +980,10 @@ class ZeroOneAdamW:
         self._grad_cache = {}
         self._staged = None
         self._landed = {}  # what was pushed early no longer matches the gradients
-        if self._land_hooks:  # (a backward that raised may have left both behind)
+        if self._lland:
+            self._lland_stream.synchronize()  # the arenas are rewritten by the next landings
+            self._lland_reset()
+        elif self._land_hooks:  # (a backward that raised may have left both behind)
             self._land_pending, self._land_pending_bytes = [], 0
             self._land_callback = False
         for parameter in self.params:
@@ -965,7 +1102,23 @@ class ZeroOneAdamW:
             self._fused_sumsq = None
             reuse = fused is not None and all(
                 self.params[i].grad is g for g, i in zip(fused, (i for c in self._classes for i in c.owned)))
-            if not reuse:
+            landed = False
+            if self._lland:  # world 1: the square sums taken while the gradients landed
+                self._lland_flush()
+                self._lland_callback = False
+                landed = self._lland_ready()
+            if landed:
+                main = torch.cuda.current_stream()
+                main.wait_stream(self._lland_stream)
+                n_slots = self._lland_slots
+                self._lland_out_host[:n_slots].copy_(self._lland_out[:n_slots], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record()
+                self._stage_step()
+                ev.synchronize()
+                partial = self._lland_out_host[:n_slots].tolist()
+                self.land_norm_steps += 1
+            elif not reuse:
                 keep = []  # contiguous copies of strided gradients must outlive the launches
                 for k, c in enumerate(self._classes):
                     grads, ptrs = self._cached_grads(k, c)
@@ -979,7 +1132,9 @@ class ZeroOneAdamW:
                               self._stream())
                     self.launches += 2 if n else 1
                 self._phase("sumsq", False)
-            if self.world > 1 and reuse:  # the exchange's square sums, one per class and round
+            if landed:
+                pass
+            elif self.world > 1 and reuse:  # the exchange's square sums, one per class and round
                 self._comm.all_reduce_sum(self._norm_rounds, HA_F64)
                 self._stage_step()
                 partial = self._comm.read(self._norm_rounds, self._norm_rounds_host,
@@ -1010,6 +1165,8 @@ class ZeroOneAdamW:
             return
         scale, self._pending_clip = self._pending_clip, None
         self._fused_sumsq = None  # the gradients change below
+        if self._lland:
+            self._lland_valid = False  # (in place, by this library's kernel: torch sees no new version)
         self._grad_cache = {}
         with torch.cuda.device(self.device):
             keep = []

@@ -148,6 +148,14 @@ int ha_adamw_step(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t 
 int ha_grad_sumsq(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks, int64_t chunk_elems,
                   int grad_dtype, double* d_partials, double* d_out, void* stream);
 
+/* ha_grad_sumsq on at most max_ctas CTAs (0: one per chunk, as ha_grad_sumsq), each taking
+ * every max_ctas-th chunk.  For a sum launched beside other kernels (the square sums taken
+ * while backward still runs, at world size 1), which a capped grid leaves most SMs to.  The
+ * partials and the result are the same, bit for bit, for every max_ctas.  No counterpart in
+ * the reference. */
+int ha_grad_sumsq_ctas(const ha_tensor* d_tensors, const ha_chunk* d_chunks, int64_t n_chunks, int64_t chunk_elems,
+                       int grad_dtype, double* d_partials, double* d_out, int max_ctas, void* stream);
+
 /* Allocation-free ha_grad_sumsq, for callers that cannot allocate device scratch (an
  * engine whose pools already hold nearly all of HBM, a loop that must avoid the implicit
  * synchronization of cudaMalloc / cudaFree, a host binding without a device allocator).

@@ -112,5 +112,7 @@ def test_kernel_entry_points_validate_arguments_without_a_gpu():
     _lib.call("ha_copy_async", _lib.np_ptr(same), 1, 2, None)  # src == dst: skipped, no CUDA call
     with pytest.raises(_lib.HAError):
         _lib.call("ha_grad_sumsq", None, None, 5, _lib.HA_SUMSQ_CHUNK, _lib.HA_BF16, None, None, None)
+    with pytest.raises(_lib.HAError, match="max_ctas"):
+        _lib.call("ha_grad_sumsq_ctas", None, None, 5, _lib.HA_SUMSQ_CHUNK, _lib.HA_BF16, None, None, -1, None)
     with pytest.raises(_lib.HAError):
         _lib.call("ha_reduce_scatter", None, None, None, 1, _lib.HA_BF16, None)

@@ -165,6 +165,33 @@ def test_grad_sumsq(code):
     assert abs(results[0] - exact) <= 1e-7 * exact
 
 
+@pytest.mark.parametrize("code", [BF16, F32], ids=["bf16", "f32"])
+def test_grad_sumsq_capped_grid_is_bit_identical(code):
+    """ha_grad_sumsq_ctas: every CTA cap (1, a few, fewer than the chunks, more than the
+    chunks) gives the partials and the sum of the one-CTA-per-chunk launch, bit for bit."""
+    import torch
+    ts = Tensors(code, SIZES + [5 * 32768 + 3], seed=31 + code, misalign=(6,), no_grad=(1,))
+    table = ts.device_table(0.0)
+    chunks = layout.chunk_table(ts.sizes, _lib.HA_SUMSQ_CHUNK)
+    dchunks = _dev_bytes(chunks)
+    n = len(chunks)
+    base_p = torch.empty(n, dtype=torch.float64, device="cuda")
+    base = torch.empty(1, dtype=torch.float64, device="cuda")
+    _lib.call("ha_grad_sumsq", table.data_ptr(), dchunks.data_ptr(), n, _lib.HA_SUMSQ_CHUNK, code,
+              base_p.data_ptr(), base.data_ptr(), _stream())
+    for cap in (1, 3, 16, max(n - 1, 1), n + 7, 0):
+        p = torch.full((n,), float("nan"), dtype=torch.float64, device="cuda")
+        out = torch.empty(1, dtype=torch.float64, device="cuda")
+        _lib.call("ha_grad_sumsq_ctas", table.data_ptr(), dchunks.data_ptr(), n, _lib.HA_SUMSQ_CHUNK, code,
+                  p.data_ptr(), out.data_ptr(), cap, _stream())
+        torch.cuda.synchronize()
+        assert torch.equal(p.view(torch.int64), base_p.view(torch.int64)), cap
+        assert out.item() == base.item(), cap
+    with pytest.raises(RuntimeError):
+        _lib.call("ha_grad_sumsq_ctas", table.data_ptr(), dchunks.data_ptr(), n, _lib.HA_SUMSQ_CHUNK, code,
+                  base_p.data_ptr(), base.data_ptr(), -1, _stream())
+
+
 def test_grad_sumsq_nonfinite_and_empty():
     import torch
     ts = Tensors(BF16, [1000, 70000], seed=9)

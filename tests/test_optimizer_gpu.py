@@ -338,3 +338,51 @@ def test_staged_tables_follow_changes_and_skips():
         assert_bits_equal(to_numpy(opt.exp_avg[i], 0), m, f"exp_avg[{i}]")
         assert_bits_equal(to_numpy(opt.exp_avg_sq[i], 0), v, f"exp_avg_sq[{i}]")
         assert_bits_equal(to_numpy(params[i].data, case.dtype), ora.params[i], f"param[{i}]")
+
+
+def _backward_into(params, grads, case, parts=1):
+    """Gradients produced by autograd: ``parts`` backward passes of sum(p * g / parts) (exact in
+    binary floating point), so each parameter's gradient equals g."""
+    import torch
+    half = [None if g is None else to_torch(g, case.dtype, p.shape, "cuda") * (1.0 / parts)
+            for p, g in zip(params, grads)]
+    for _ in range(parts):
+        terms = [(p * h).sum() for p, h in zip(params, half) if h is not None]
+        if terms:
+            torch.autograd.backward(terms)
+
+
+def test_landing_at_world_one_takes_the_norm_as_gradients_land():
+    """land_grads=True at world size 1: the square sums are taken while backward runs and
+    clip_grad_norm only adds them; norms and every state bit equal the oracle replaying them, and
+    a gradient landed twice (two backward passes) or changed in place after landing falls back to
+    the full pass with the same results."""
+    import torch
+    case = next(c for c in CASES if c.name == "bf16_clip")
+    params, opt = build(case, land_grads=True)
+    ref_params, ref = build(case)
+    norms = []
+    for s in range(case.steps):
+        grads = case.grads(s, 0)
+        for ps, o in ((params, opt), (ref_params, ref)):
+            o.zero_grad(set_to_none=True)
+            _backward_into(ps, grads, case, parts=2 if (s == 1 and o is opt) else 1)
+            if s == 2 and o is opt:
+                params[0].grad.mul_(1.0)  # in place after landing: its version moves
+            o.all_reduce_grads()
+            n = o.clip_grad_norm(case.max_norm)
+            if o is opt:
+                norms.append(n)
+            else:
+                assert abs(n - norms[-1]) <= 1e-6 * n, (s, n, norms[-1])
+            o.step()
+    torch.cuda.synchronize()
+    assert opt.land_norm_steps == 1  # step 0 landed; step 1 landed twice, step 2 changed: full passes
+    ora, _ = oracle_replay(case, Z.FORM_TORCH_CUDA, norms=norms)
+    for i in range(len(case.shapes)):
+        master, m, v, _ = ora.tensor_state(i)
+        assert_bits_equal(to_numpy(opt.master[i], 0), master, f"master[{i}]")
+        assert_bits_equal(to_numpy(opt.exp_avg[i], 0), m, f"exp_avg[{i}]")
+        assert_bits_equal(to_numpy(opt.exp_avg_sq[i], 0), v, f"exp_avg_sq[{i}]")
+        assert_bits_equal(to_numpy(params[i].data, case.dtype), ora.params[i], f"param[{i}]")
+    opt.close()
