@@ -72,7 +72,10 @@ def assert_state_close(a: np.ndarray, b: np.ndarray, what: str, *, max_ulp: int 
     kernels round the update term ``lr * m_hat / (sqrt(v_hat) + eps)`` differently
     (optimizer.py:188-189: ``x / c`` vs ``x * (1 / c)``, MKL's sqrt, ``addcdiv_``'s two forms), by
     up to an ulp of ``lr`` per step; a master within a few updates of zero then differs by more
-    than 2 of its own ulps.  Such elements pass if ``|a - b| <= k`` ulps of ``lr``."""
+    than 2 of its own ulps.  Such elements pass if ``|a - b| <= k`` ulps of ``lr``.  ``lr`` may be
+    an array, per element the magnitude of that element's update term, where it exceeds ``lr``
+    (``m_hat / sqrt(v_hat)`` above 1): a rounding of the term then moves the master by an ulp of
+    the term."""
     a = np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
     b = np.ascontiguousarray(b, dtype=np.float32).reshape(-1)
     ulp = Z.ulp_distance(a, b)
@@ -82,7 +85,7 @@ def assert_state_close(a: np.ndarray, b: np.ndarray, what: str, *, max_ulp: int 
     ok = (ulp <= max_ulp) | (fin & (rel_err <= rel))
     if lr_ulps is not None:
         lr, k = lr_ulps
-        ok |= fin & (diff <= k * float(np.spacing(np.float32(lr))))
+        ok |= fin & (diff <= k * np.spacing(np.abs(np.asarray(lr, dtype=np.float32))).astype(np.float64))
     bad = ~ok
     assert not bad.any(), (f"{what}: {int(bad.sum())} of {a.size} elements outside {max_ulp} ulp / rel {rel}"
                            f"{'' if lr_ulps is None else f' / {lr_ulps[1]} ulp(lr)'} "
