@@ -29,7 +29,12 @@ Printed (rank 0, one JSON line):
   cpu_baseline the reference's own optimizer (staged unmodified by oracle/stage_ref.py) on
                this host's CPU cores (N=1, rank 0), on a bounded sample of the same
                parameter set (configuration 1: the whole of it);
-  clocks       nvidia-smi samples taken during the timed region.
+  clocks       nvidia-smi samples taken during the timed region;
+  iteration_with_backward
+               N > 1, after the above: forward + backward + optimizer per iteration with
+               gradient landing off and on the copy engines (measure_landing, the ``--landing``
+               synthetic backward over ``--tokens`` tokens), on a second optimizer built once
+               the timed one is released.
 ``--impl reference`` times only that CPU implementation (rank 0; other ranks exit), for the
 steps and warm-up it prints, plus BASELINE configuration 1 whole (``config1``).
 ``--probe-links`` (N > 1) measures NVLink bandwidth between the GPUs instead.
@@ -84,6 +89,8 @@ def parse_args():
     ap.add_argument("--cpu-sample-params", type=int, default=200_000_000)
     ap.add_argument("--max-params", type=int, default=0, help="truncate the parameter set (smoke / profiling)")
     ap.add_argument("--landing", action="store_true", help="measure gradient landing")
+    ap.add_argument("--no-landing", action="store_true", help="N > 1: leave out the iteration_with_backward "
+                    "measurement of the step's JSON line")
     ap.add_argument("--tokens", type=int, default=2048, help="tokens of the --landing synthetic backward")
     ap.add_argument("--probe-links", action="store_true", help="measure NVLink bandwidth between the N GPUs")
     ap.add_argument("--probe-bytes", type=int, default=2 << 30, help="--probe-links: bytes each rank moves")
@@ -684,10 +691,30 @@ def run_ours(args) -> None:
                 cpu_sample(args.workload, args.cpu_sample_params, steps=4, warmup=1))
         cpu = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample", "impl", "ms_per_step")}
 
+    # ---- the whole iteration at N > 1: a synthetic backward + the optimizer, gradient landing off
+    # and on, on a second optimizer built once this one is released (not part of the timed step)
+    landing = None
+    if world > 1 and not args.no_landing and not fp32_set:
+        from types import SimpleNamespace
+        barrier()
+        info = SimpleNamespace(comm_mode=opt.comm_mode, push_streams=opt.push_streams, push_ctas=opt.push_ctas,
+                               gather_mode=opt.gather_mode)
+        opt.close()
+        opt = info
+        params = inputs = None
+        import gc
+        gc.collect()
+        torch.cuda.empty_cache()
+        try:
+            landing = measure_landing(args, shapes, dev, rank, world, [0], min(args.steps, 5))
+        except torch.OutOfMemoryError as e:  # every rank allocates the same sizes, so all raise together
+            landing = {"error": f"out of device memory: {str(e).splitlines()[0]}"}
+
     if rank != 0:
         if world > 1:
             dist.barrier()
-            opt.close()
+            if landing is None:
+                opt.close()
             dist.destroy_process_group()
         return
     peak, peak_kind = measured_hbm_peak()
@@ -783,44 +810,45 @@ def run_ours(args) -> None:
         "e2e": e2e,
         "clocks": clock,
         "gpu_launches": launches,
+        "iteration_with_backward": landing,
     }
     print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()
-        opt.close()
+        if landing is None:
+            opt.close()
         dist.destroy_process_group()
 
 
-def run_landing(args) -> None:
-    """Gradient landing: forward + backward + optimizer step, landing off vs on (N > 1: the early
-    pushes of the exchange; N = 1: the norm's square sums taken as the gradients land)."""
+def measure_landing(args, shapes, dev, rank: int, world: int, caps: list[int], steps: int) -> dict:
+    """Forward + backward + optimizer iterations with gradient landing off and on, on a fresh
+    optimizer built with ``land_grads=True`` (N > 1: the early pushes of the exchange, receive
+    window sized for two rounds; N = 1: the norm's square sums taken as the gradients land).
+    The synthetic backward: one ``linear`` per matrix over ``args.tokens`` tokens, a dot product
+    per vector.  Per variant the forward + backward time, the optimizer time left after
+    backward, and their sum, CUDA events, mean over ``steps``, max over ranks."""
     import torch
     import torch.distributed as dist
     import torch.nn.functional as F
 
-    from hybridagent_b200 import ZeroOneAdamW, workloads
+    from hybridagent_b200 import ZeroOneAdamW
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
-    shapes = workloads.WORKLOADS[args.workload]()
-    if args.max_params:
-        shapes = workloads.truncated(shapes, args.max_params)
     n_params = sum(math.prod(s) for s in shapes)
-    # a receive window of two rounds: every piece may be pushed while its gradient lands
+    window = 2 * n_params + (256 << 20) if world > 1 else 0  # every piece may be pushed as it lands
+    saved = os.environ.get("HYBRIDAGENT_B200_RECV_BYTES")
     if world > 1:
-        os.environ["HYBRIDAGENT_B200_RECV_BYTES"] = str(2 * n_params + (256 << 20))
+        os.environ["HYBRIDAGENT_B200_RECV_BYTES"] = str(window)
     gen = torch.Generator(device=dev).manual_seed(1234)
     params = [torch.nn.Parameter((torch.randn(s, device=dev, generator=gen) * 0.02).to(torch.bfloat16))
               for s in shapes]
-    opt = ZeroOneAdamW([{"params": params, "lr": 1e-6}], rank=rank, world_size=world, weight_decay=0.01,
-                       land_grads=True)
+    try:
+        opt = ZeroOneAdamW([{"params": params, "lr": 1e-6}], rank=rank, world_size=world, weight_decay=0.01,
+                           land_grads=True)
+    finally:
+        if saved is None:
+            os.environ.pop("HYBRIDAGENT_B200_RECV_BYTES", None)
+        else:
+            os.environ["HYBRIDAGENT_B200_RECV_BYTES"] = saved
     gx = torch.Generator(device=dev).manual_seed(777 + rank)
     T = args.tokens
     dims_in = sorted({s[1] for s in shapes if len(s) == 2})
@@ -849,15 +877,15 @@ def run_landing(args) -> None:
         opt.step()
         ev[2].record()
 
+    warm = max(args.warmup, 3)
     out = {}
-    caps = [int(x) for x in args.land_ctas.split(",")]
     for variant in ["off"] + [f"on_ctas{n}" for n in caps]:
         opt.landing_enabled = variant != "off"
         if opt.landing_enabled:  # N > 1: CTAs of the early pushes; N = 1: of the square sums
             opt.land_ctas = int(variant[len("on_ctas"):])
         launches0 = opt.land_launches if world > 1 else opt.land_norm_steps
-        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-        for _ in range(max(args.warmup, 3)):
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+        for _ in range(warm):
             one([torch.cuda.Event(enable_timing=True) for _ in range(3)])
         if world > 1:
             dist.barrier()
@@ -872,26 +900,52 @@ def run_landing(args) -> None:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         out[variant] = {"fwd_bwd_ms": round(float(t[0]), 3), "step_after_backward_ms": round(float(t[1]), 3),
                         "total_ms": round(float(t[2]), 3)}
-        n_steps = len(evs) + max(args.warmup, 3)
         if world > 1:
-            out[variant]["early_push_calls_per_step"] = (opt.land_launches - launches0) // n_steps
+            out[variant]["early_push_calls_per_step"] = (opt.land_launches - launches0) // (len(evs) + warm)
         else:
-            out[variant]["landed_norm_steps"] = f"{opt.land_norm_steps - launches0}/{n_steps}"
-    best = min((k for k in out if k != "off"), key=lambda k: out[k]["total_ms"])
-    if rank == 0:
-        line = {"metric": "fwd_bwd_plus_step_ms", "value": out[best]["total_ms"], "unit": "ms", "n_gpus": world,
-                "steps": args.steps, "warmup": max(args.warmup, 3), "higher_is_better": False, "scaling": "strong",
-                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": args.workload, "params": n_params, "tensors": len(shapes), "tokens": T,
-                           "recv_window_bytes": int(os.environ["HYBRIDAGENT_B200_RECV_BYTES"]) if world > 1 else 0,
-                           "comm_mode": opt.comm_mode, "parallelism": f"zero1-dp{world}"},
-                "landing": out, "best": best,
-                "saved_ms": round(out["off"]["total_ms"] - out[best]["total_ms"], 3)}
-        print(json.dumps(line), flush=True)
+            out[variant]["landed_norm_steps"] = f"{opt.land_norm_steps - launches0}/{len(evs) + warm}"
+    comm_mode = opt.comm_mode
     if world > 1:
         dist.barrier()
     opt.close()
+    best = min((k for k in out if k != "off"), key=lambda k: out[k]["total_ms"])
+    return {"variants": out, "best": best, "saved_ms": round(out["off"]["total_ms"] - out[best]["total_ms"], 3),
+            "steps": steps, "warmup": warm, "tokens": T, "recv_window_bytes": window, "comm_mode": comm_mode}
+
+
+def run_landing(args) -> None:
+    """``--landing``: prints measure_landing's result for the workload as its own JSON line."""
+    import torch
+    import torch.distributed as dist
+
+    from hybridagent_b200 import workloads
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
     if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    shapes = workloads.WORKLOADS[args.workload]()
+    if args.max_params:
+        shapes = workloads.truncated(shapes, args.max_params)
+    res = measure_landing(args, shapes, dev, rank, world, [int(x) for x in args.land_ctas.split(",")], args.steps)
+    if rank == 0:
+        out, best = res["variants"], res["best"]
+        line = {"metric": "fwd_bwd_plus_step_ms", "value": out[best]["total_ms"], "unit": "ms", "n_gpus": world,
+                "steps": args.steps, "warmup": res["warmup"], "higher_is_better": False, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": args.workload, "params": sum(math.prod(s) for s in shapes),
+                           "tensors": len(shapes), "tokens": res["tokens"],
+                           "recv_window_bytes": res["recv_window_bytes"],
+                           "comm_mode": res["comm_mode"], "parallelism": f"zero1-dp{world}"},
+                "landing": out, "best": best, "saved_ms": res["saved_ms"]}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 
