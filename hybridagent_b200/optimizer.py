@@ -1108,53 +1108,57 @@ class ZeroOneAdamW:
                 self._lland_callback = False
                 landed = self._lland_ready()
             if landed:
-                main = torch.cuda.current_stream()
-                main.wait_stream(self._lland_stream)
+                torch.cuda.current_stream().wait_stream(self._lland_stream)
                 n_slots = self._lland_slots
-                self._lland_out_host[:n_slots].copy_(self._lland_out[:n_slots], non_blocking=True)
-                ev = torch.cuda.Event()
-                ev.record()
-                self._stage_step()
-                ev.synchronize()
-                partial = self._lland_out_host[:n_slots].tolist()
+                partial = self._read_local(self._lland_out[:n_slots], self._lland_out_host[:n_slots])
                 self.land_norm_steps += 1
-            elif not reuse:
-                keep = []  # contiguous copies of strided gradients must outlive the launches
-                for k, c in enumerate(self._classes):
-                    grads, ptrs = self._cached_grads(k, c)
-                    keep.append(grads)
-                    self._upload_table(c, ptrs, advance=False)
-                self._phase("sumsq", True)
-                for k, c in enumerate(self._classes):
-                    chunks, n = c.sumsq_chunks
-                    _lib.call("ha_grad_sumsq", c.table.ptr, None if chunks is None else chunks.data_ptr(), n,
-                              HA_SUMSQ_CHUNK, c.code, c.partials.data_ptr(), self._norm_buf[k:].data_ptr(),
-                              self._stream())
-                    self.launches += 2 if n else 1
-                self._phase("sumsq", False)
-            if landed:
-                pass
-            elif self.world > 1 and reuse:  # the exchange's square sums, one per class and round
-                self._comm.all_reduce_sum(self._norm_rounds, HA_F64)
-                self._stage_step()
-                partial = self._comm.read(self._norm_rounds, self._norm_rounds_host,
-                                          "all-reduce(sum) of the norm").reshape(-1).tolist()
-            elif self.world > 1:
-                self._comm.all_reduce_sum(self._norm_buf, HA_F64)
-                self._stage_step()
-                partial = self._comm.read(self._norm_buf, self._norm_host, "all-reduce(sum) of the norm").tolist()
             else:
-                self._norm_host.copy_(self._norm_buf, non_blocking=True)
-                ev = torch.cuda.Event()
-                ev.record()
-                self._stage_step()
-                ev.synchronize()
-                partial = self._norm_host.tolist()
+                # (the contiguous copies of strided gradients must outlive the launches)
+                keep = None if reuse else self._launch_sumsq()  # noqa: F841
+                if self.world > 1 and reuse:  # the exchange's square sums, one per class and round
+                    self._comm.all_reduce_sum(self._norm_rounds, HA_F64)
+                    self._stage_step()
+                    partial = self._comm.read(self._norm_rounds, self._norm_rounds_host,
+                                              "all-reduce(sum) of the norm").reshape(-1).tolist()
+                elif self.world > 1:
+                    self._comm.all_reduce_sum(self._norm_buf, HA_F64)
+                    self._stage_step()
+                    partial = self._comm.read(self._norm_buf, self._norm_host,
+                                              "all-reduce(sum) of the norm").tolist()
+                else:
+                    partial = self._read_local(self._norm_buf, self._norm_host)
         total = np.float32(sum(partial))  # the reference's total is an fp32 tensor
         norm = float(np.sqrt(total))      # float(total.sqrt()), optimizer.py:154
         if max_norm > 0 and norm > max_norm:
             self._pending_clip = float(max_norm) / (norm + 1e-6)  # optimizer.py:156
         return norm
+
+    def _launch_sumsq(self) -> list:
+        """One ``ha_grad_sumsq`` per dtype class over its owned gradients into ``_norm_buf``;
+        returns the gradient lists, whose contiguous copies must outlive the launches."""
+        keep = []
+        for k, c in enumerate(self._classes):
+            grads, ptrs = self._cached_grads(k, c)
+            keep.append(grads)
+            self._upload_table(c, ptrs, advance=False)
+        self._phase("sumsq", True)
+        for k, c in enumerate(self._classes):
+            chunks, n = c.sumsq_chunks
+            _lib.call("ha_grad_sumsq", c.table.ptr, None if chunks is None else chunks.data_ptr(), n,
+                      HA_SUMSQ_CHUNK, c.code, c.partials.data_ptr(), self._norm_buf[k:].data_ptr(), self._stream())
+            self.launches += 2 if n else 1
+        self._phase("sumsq", False)
+        return keep
+
+    def _read_local(self, dev: torch.Tensor, host: torch.Tensor) -> list:
+        """World size 1: copies the fp64 sums to pinned host memory, stages the next step's
+        tables while the copy is in flight, and returns the sums."""
+        host.copy_(dev, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._stage_step()
+        ev.synchronize()
+        return host.tolist()
 
     @_nvtx
     @torch.no_grad()
