@@ -675,6 +675,9 @@ def run_ours(args) -> None:
         e2e_ms = float(te[0])
         e2e = {"value": round(n_params / (e2e_ms * 1e-3) / 1e9, 3), "unit": "Gparams/s", "ms_per_step": round(e2e_ms, 3),
                "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
+               "bound": "PCIe: the host-to-device copy of the step's gradients" if world == 1 else
+                        f"the host: all {world} ranks copy the whole model's gradients out of one host's pinned "
+                        "memory at once",
                "how": f"host wall clock over {args.e2e_steps} steps; every step copies all gradients from pinned host "
                       f"memory (per-tensor cudaMemcpyAsync, {how}) and reads the norm back in clip_grad_norm"}
         del spare, bufs
