@@ -326,8 +326,9 @@ class ZeroOneAdamW:
                  land_grads: bool = False):
         # argument handling and errors as optimizer.py:24-44; comm_timeout_s (world > 1): seconds a
         # collective may wait for the other ranks before the communicator is aborted and the call
-        # raises CommFailure (default HYBRIDAGENT_B200_COMM_TIMEOUT_S or 1800); land_grads (world > 1,
-        # p2p mode): push gradients to their owners while backward is still running
+        # raises CommFailure (default HYBRIDAGENT_B200_COMM_TIMEOUT_S or 1800); land_grads: while
+        # backward is still running, push gradients to their owners (world > 1, p2p mode) or take
+        # the norm's square sums (world 1)
         self.rank = int(rank)
         self.world = int(world_size)
         self.betas = tuple(float(value) for value in betas)
