@@ -43,20 +43,21 @@ class Heartbeat:
         """Bumps this rank's counter and reads the peers' (the thread does both every
         interval, so a peer's counter is watched continuously, not only when asked)."""
         self._beats += 1
-        keys = [self.keys[r] for r in self.peers]
         try:
             with self._lock:
                 self.store.set(self.keys[self.rank], str(self._beats))
-                # check() first: multi_get would block on a key a peer has not written yet
-                values = self.store.multi_get(keys) if self.store.check(keys) else None
+                # check() each key first: a get would block on a key its peer has not written yet,
+                # and one late peer must not hide the counters of the others
+                present = [r for r in self.peers if self.store.check([self.keys[r]])]
+                values = self.store.multi_get([self.keys[r] for r in present]) if present else []
         except Exception as e:  # noqa: BLE001 -- any store failure means the peers cannot be trusted
             self.failed = f"heartbeat store: {e}"
             return
         now = time.monotonic()
         with self._lock:
-            for k, r in enumerate(self.peers):
-                value = None if values is None else bytes(values[k])
-                if value is not None and value != self._seen[r][0]:
+            for r, value in zip(present, values):
+                value = bytes(value)
+                if value != self._seen[r][0]:
                     self._seen[r] = (value, now)
 
     def _run(self) -> None:

@@ -14,8 +14,8 @@ from hybridagent_b200.liveness import Heartbeat
 
 def test_stopped_heartbeat_goes_stale_in_one_store():
     store = dist.HashStore()
-    a = Heartbeat(store, 0, 2, interval_s=0.05, deadline_s=0.4)
-    b = Heartbeat(store, 1, 2, interval_s=0.05, deadline_s=0.4)
+    a = Heartbeat(store, 0, 2, interval_s=0.05, deadline_s=1.0)
+    b = Heartbeat(store, 1, 2, interval_s=0.05, deadline_s=1.0)
     try:
         time.sleep(0.2)
         assert a.stale_peers() == [] and b.stale_peers() == []
@@ -23,7 +23,7 @@ def test_stopped_heartbeat_goes_stale_in_one_store():
             time.sleep(0.15)
             assert a.all_fresh()
         b.stop()  # rank 1 stalls: its counter stops moving
-        time.sleep(0.6)
+        time.sleep(1.6)
         assert a.stale_peers() == [1]
     finally:
         a.stop()
@@ -32,14 +32,16 @@ def test_stopped_heartbeat_goes_stale_in_one_store():
 
 def test_missing_peer_is_stale_after_the_deadline():
     store = dist.HashStore()
-    a = Heartbeat(store, 0, 3, interval_s=0.05, deadline_s=0.3)
+    a = Heartbeat(store, 0, 3, interval_s=0.05, deadline_s=1.0)
+    c = Heartbeat(store, 2, 3, interval_s=0.05, deadline_s=1.0)  # rank 1 never starts
     try:
-        Heartbeat(store, 2, 3, interval_s=0.05, deadline_s=0.3)  # rank 1 never starts
         assert a.stale_peers() == []  # within the deadline of construction
-        time.sleep(0.5)
-        assert 1 in a.stale_peers()
+        time.sleep(1.6)
+        assert a.stale_peers() == [1]  # the late peer hides nothing: rank 2 is seen beating
+        assert c.stale_peers() == [1]
     finally:
         a.stop()
+        c.stop()
 
 
 def _free_port() -> int:
@@ -52,7 +54,7 @@ def _rank(rank: int, port: int, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=2)
     store = dist.distributed_c10d._get_default_store()
-    hb = Heartbeat(store, rank, 2, interval_s=0.05, deadline_s=0.5)
+    hb = Heartbeat(store, rank, 2, interval_s=0.05, deadline_s=1.0)
     try:
         dist.barrier()
         time.sleep(0.3)
@@ -60,10 +62,10 @@ def _rank(rank: int, port: int, q):
         dist.barrier()
         if rank == 1:
             hb.stop()  # host-side stall: rank 1 stops beating (nothing of its in flight)
-            time.sleep(1.5)
+            time.sleep(2.5)
             stale = hb.stale_peers()
         else:
-            time.sleep(1.0)
+            time.sleep(2.0)
             stale = hb.stale_peers()
         q.put((rank, fresh, stale))
         dist.barrier()
