@@ -710,8 +710,10 @@ def run_ours(args) -> None:
         torch.cuda.empty_cache()
         try:
             landing = measure_landing(args, shapes, dev, rank, world, [0], min(args.steps, 5))
-        except torch.OutOfMemoryError as e:  # every rank allocates the same sizes, so all raise together
-            landing = {"error": f"out of device memory: {str(e).splitlines()[0]}"}
+        except Exception as e:  # noqa: BLE001 -- an extra measurement after the timed region: its
+            # failure (out of memory, where every rank allocates the same sizes and all raise
+            # together) is reported in the line instead of losing the line
+            landing = {"error": f"{type(e).__name__}: {(str(e).splitlines() or [''])[0]}"}
 
     if rank != 0:
         if world > 1:
