@@ -125,11 +125,12 @@ def peer_deltas(param_bases: list[int], rank: int) -> list[int]:
 class Pieces:
     """The parts of a dtype class's gradients that one exchange round moves.
 
-    Round k covers elements [k*S, (k+1)*S) of every owner's segment (S = round_elems), so a
-    tensor whose slot crosses a multiple of S is split.  Entry j: element ``src_off[j]`` of
-    table entry ``tensor[j]`` (an index into ``cls.indices``), ``count[j]`` elements, owned
-    by ``owner[j]``, landing at element ``dst_off[j]`` of the sender's region of that
-    round's receive window; ``round[j]`` is its round."""
+    Round k covers elements [bounds[k], bounds[k+1]) of every owner's segment, at most
+    S = round_elems of them (round_bounds: k*S, unless the last round is split), so a tensor
+    whose slot crosses a bound is split.  Entry j: element ``src_off[j]`` of table entry
+    ``tensor[j]`` (an index into ``cls.indices``), ``count[j]`` elements, owned by
+    ``owner[j]``, landing at element ``dst_off[j]`` of the sender's region (S elements) of
+    that round's receive window; ``round[j]`` is its round."""
     tensor: np.ndarray
     src_off: np.ndarray
     owner: np.ndarray
@@ -138,11 +139,36 @@ class Pieces:
     round: np.ndarray
     n_rounds: int
     round_elems: int
+    bounds: np.ndarray
 
     def own_counts(self, cls: DtypeClass, rank: int) -> list[int]:
         """Elements of ``rank``'s segment each round reduces (its padded load, split)."""
-        S, n = self.round_elems, cls.own_len[rank]
-        return [max(0, min(S, n - k * S)) for k in range(self.n_rounds)]
+        b, n = self.bounds, cls.own_len[rank]
+        return [max(0, min(int(b[k + 1]), n) - int(b[k])) for k in range(self.n_rounds)]
+
+
+def round_bounds(seg_len: int, S: int, tail_split: int = 0) -> np.ndarray:
+    """Start of every exchange round in each owner's segment, then the end of the last one.
+
+    Rounds of S elements; with ``tail_split`` = t > 0 the last round's part of the segment is
+    cut into up to t + 1 rounds of halving length (1/2, 1/4, ... of it, multiples of ALIGN, the
+    last taking the rest).  The owner's sum of the last round runs after every push, with
+    nothing left to overlap it, so a short last round shortens the step by most of that sum,
+    at the cost of t more rounds (a barrier and a sum launch each)."""
+    assert S % ALIGN == 0 and S > 0
+    n = max(1, -(-seg_len // S))
+    bounds = [k * S for k in range(n)]
+    last = bounds[-1]
+    rest = max(seg_len - last, 0)
+    for _ in range(max(tail_split, 0)):
+        part = align_up(-(-rest // 2))
+        if rest <= ALIGN or part >= rest:
+            break
+        last += part
+        rest -= part
+        bounds.append(last)
+    bounds.append(max(n * S, last + ALIGN))
+    return np.asarray(bounds, dtype=np.int64)
 
 
 def round_elems_for(cls: DtypeClass, world: int, elem_bytes: int, budget_bytes: int) -> int:
@@ -153,21 +179,25 @@ def round_elems_for(cls: DtypeClass, world: int, elem_bytes: int, budget_bytes: 
     return min(s, max(cls.seg_len, ALIGN))
 
 
-def exchange_pieces(cls: DtypeClass, owner: list[int], numels: list[int], round_elems: int) -> Pieces:
+def exchange_pieces(cls: DtypeClass, owner: list[int], numels: list[int], round_elems: int,
+                    tail_split: int = 0) -> Pieces:
     """Pieces of every tensor's slot, plus zero-fill pieces (``tensor`` -1) over the gaps
     between slots up to each owner's padded load: the two halves of the receive window are
     reused by rounds with different layouts, so every element an owner adds must be
     rewritten by every round (a gap left untouched would still hold an older round's
-    values)."""
+    values).  Rounds as ``round_bounds(cls.seg_len, round_elems, tail_split)``."""
     S = round_elems
-    assert S % ALIGN == 0
+    bounds = round_bounds(cls.seg_len, S, tail_split)
     cols = [[] for _ in range(6)]
 
     def emit(k, start, n, o, src0):
-        for r in range(start // S, (start + n - 1) // S + 1):
-            lo, hi = max(start, r * S), min(start + n, (r + 1) * S)
-            for col, val in zip(cols, (k, src0 + lo - start, o, lo - r * S, hi - lo, r)):
+        r = int(np.searchsorted(bounds, start, side="right")) - 1
+        lo = start
+        while lo < start + n:
+            hi = min(start + n, int(bounds[r + 1]))
+            for col, val in zip(cols, (k, src0 + lo - start, o, lo - int(bounds[r]), hi - lo, r)):
                 col.append(val)
+            lo, r = hi, r + 1
 
     ends = {}
     for k, i in enumerate(cls.indices):
@@ -182,8 +212,7 @@ def exchange_pieces(cls: DtypeClass, owner: list[int], numels: list[int], round_
                 emit(-1, pos, lo - pos, o, 0)
             pos = max(pos, hi)
     arr = [np.asarray(c, dtype=np.int64) for c in cols]
-    n_rounds = max(1, -(-cls.seg_len // S))
-    return Pieces(*arr, n_rounds=n_rounds, round_elems=S)
+    return Pieces(*arr, n_rounds=len(bounds) - 1, round_elems=S, bounds=bounds)
 
 
 LAND_ROUNDS = 2  # exchange rounds whose window halves are free between one update and the next exchange

@@ -233,16 +233,16 @@ class _Class:
         """p2p (peers' receive windows and parameter buffers mapped) or the local nccl pack.
 
         p2p: this rank's gradients move to their owners in rounds (layout.exchange_pieces):
-        round k covers elements [k*S, (k+1)*S) of every owner's segment and lands in half
-        k % 2 of the owner's double-buffered receive window, region <this rank>; the owner
-        adds the regions into ``own_grad``.  nccl: the whole owner-major pack of W segments
+        round k covers elements [bounds[k], bounds[k+1]) of every owner's segment (k*S, unless
+        the last round is split) and lands in half k % 2 of the owner's double-buffered receive
+        window, region <this rank> of S elements; the owner adds the regions into ``own_grad``.  nccl: the whole owner-major pack of W segments
         is reduce-scattered in place."""
         cls, W, r, dev = self.layout, opt.world, opt.rank, opt.device
         numel = opt._numels
         esz = self.packed_param.element_size()
         if recv_bases is not None:
             S = self.round_elems
-            pc = layout.exchange_pieces(cls, opt.owner, numel, S)
+            pc = layout.exchange_pieces(cls, opt.owner, numel, S, opt.tail_split)
             self.pieces = pc
             self.own_grad = torch.zeros(max(cls.own_len[r], layout.ALIGN), dtype=self.dtype, device=dev)
             base = self.own_grad
@@ -468,6 +468,11 @@ class ZeroOneAdamW:
         if self.gather_mode not in ("kernel", "ce"):
             raise ValueError(f"HYBRIDAGENT_B200_GATHER={self.gather_mode!r}: expected kernel or ce")
         self.gather_part_bytes = int(os.environ.get("HYBRIDAGENT_B200_GATHER_PART_BYTES", str(128 << 20)))
+        # the last exchange round cut into up to this many more rounds of halving length
+        # (layout.round_bounds): the owner sum after the last push is the one nothing overlaps
+        self.tail_split = int(os.environ.get("HYBRIDAGENT_B200_TAIL_SPLIT", "0"))
+        if self.tail_split < 0:
+            raise ValueError(f"HYBRIDAGENT_B200_TAIL_SPLIT={self.tail_split}: expected >= 0")
         want = os.environ.get("HYBRIDAGENT_B200_COMM", "p2p")
         if want not in ("p2p", "nccl"):
             raise ValueError(f"HYBRIDAGENT_B200_COMM={want!r}: expected p2p or nccl")
@@ -558,7 +563,8 @@ class ZeroOneAdamW:
                     S, esz = c.round_elems, c.packed_param.element_size()
                     count = c.own_counts[k]
                     window = c.recv_buf.ptr + (k % 2) * self.world * S * esz
-                    _lib.call("ha_sum_regions", window, self.world, S, count, c.own_grad.data_ptr() + k * S * esz,
+                    own = c.own_grad.data_ptr() + int(c.pieces.bounds[k]) * esz
+                    _lib.call("ha_sum_regions", window, self.world, S, count, own,
                               c.code, c.region_partials.data_ptr(), self._norm_rounds[ci, k:].data_ptr(),
                               side.cuda_stream)
                     self.launches += 2 if count else 1

@@ -74,14 +74,18 @@ def test_push_destinations_land_in_the_senders_region():
     assert layout.peer_deltas([100, 300, 700], 1) == [-200, 400]
 
 
-@pytest.mark.parametrize("world,S", [(2, 64 * 1000), (3, 64 * 7), (8, 64 * 50_000), (2, 64)])
-def test_exchange_pieces_partition_every_slot_and_gap(world, S):
+@pytest.mark.parametrize("world,S,tail", [(2, 64 * 1000, 0), (3, 64 * 7, 0), (8, 64 * 50_000, 0), (2, 64, 0),
+                                          (2, 64 * 1000, 3), (3, 64 * 7, 2), (8, 64 * 50_000, 4), (2, 64, 3)])
+def test_exchange_pieces_partition_every_slot_and_gap(world, S, tail):
     import numpy as np
     n = [1000, 64, 5000, 3, 70000, 1, 12345, 640000]
     p = layout.plan(n, [HA_BF16] * len(n), world)
     (cls,) = p.classes
-    pc = layout.exchange_pieces(cls, p.owner, n, S)
-    assert pc.n_rounds == -(-cls.seg_len // S)
+    pc = layout.exchange_pieces(cls, p.owner, n, S, tail)
+    if tail == 0:
+        assert pc.n_rounds == -(-cls.seg_len // S)
+    else:
+        assert -(-cls.seg_len // S) <= pc.n_rounds <= -(-cls.seg_len // S) + tail
     covered = {i: np.zeros(n[i], np.int32) for i in cls.indices}
     # what each owner's region receives in each round, from every piece (tensors and gaps)
     written = {(o, r): np.zeros(S, np.int32) for o in range(world) for r in range(pc.n_rounds)}
@@ -92,7 +96,7 @@ def test_exchange_pieces_partition_every_slot_and_gap(world, S):
             continue  # a zero-filled gap
         i = cls.indices[t]
         assert o == p.owner[i]
-        assert cls.offset[i] + so == r * S + do  # same segment coordinate
+        assert cls.offset[i] + so == pc.bounds[r] + do  # same segment coordinate
         covered[i][so:so + c] += 1
     assert all((v == 1).all() for v in covered.values())
     for o in range(world):
@@ -134,8 +138,9 @@ def _emulate_gather(memory, copies, chunks, chunk_elems, esz):
     return np
 
 
-@pytest.mark.parametrize("world,S", [(2, 64 * 20), (3, 64 * 7), (2, 64 * 100_000)])
-def test_landing_then_residual_equals_plain_exchange(world, S):
+@pytest.mark.parametrize("world,S,tail", [(2, 64 * 20, 0), (3, 64 * 7, 0), (2, 64 * 100_000, 0), (2, 64 * 20, 3),
+                                          (2, 64 * 100_000, 3)])
+def test_landing_then_residual_equals_plain_exchange(world, S, tail):
     """Early pushes of landed gradients (rounds 0 and 1, in two buckets, then one tensor
     landing again with new values, as a later backward of the same step would) followed by
     the exchange's own pushes with the landed pieces skipped leave every round's window
@@ -145,7 +150,7 @@ def test_landing_then_residual_equals_plain_exchange(world, S):
     n = [1000, 64, 5000, 3, 7000, 1, 1234, 6400, 640]
     p = layout.plan(n, [HA_BF16] * len(n), world)
     (cls,) = p.classes
-    pc = layout.exchange_pieces(cls, p.owner, n, S)
+    pc = layout.exchange_pieces(cls, p.owner, n, S, tail)
     rank, esz, CH = world - 1, 2, 256
     rng = np.random.default_rng(world * S)
     present = [k != 2 for k in range(len(cls.indices))]  # entry 2 has no gradient here: zero-filled
@@ -311,3 +316,21 @@ def test_peer_groups_one_destination_per_stream():
     assert [g.tolist() for g in groups] == [[1, 4], [2, 5], [3, 7]]
     groups = layout.peer_groups(np.array([0, 2, 6]), owners, rank=2, world=4)
     assert [g.tolist() for g in groups] == [[], [0, 6], []]
+
+
+@pytest.mark.parametrize("seg_len,S,tail", [(0, 64, 3), (64, 64, 3), (6400, 640, 0), (6400, 640, 3), (6401, 640, 3),
+                                            (640 * 7 + 64, 640, 5), (1 << 30, 64 << 20, 3), (100_000, 1 << 20, 4)])
+def test_round_bounds(seg_len, S, tail):
+    b = layout.round_bounds(seg_len, S, tail)
+    n = max(1, -(-seg_len // S))
+    lens = np.diff(b)
+    assert b[0] == 0 and b[-1] >= seg_len and (lens > 0).all() and (lens <= S).all()
+    assert (b % layout.ALIGN == 0).all()
+    assert list(b[:n]) == [k * S for k in range(n)]  # full rounds unchanged
+    assert len(b) - 1 <= n + tail
+    if tail == 0:
+        assert list(b) == [k * S for k in range(n + 1)]
+    tail_lens = [min(int(hi), seg_len) - int(lo) for lo, hi in zip(b[n - 1:-1], b[n:]) if lo < seg_len]
+    if len(tail_lens) > 1:  # each split part at most half of what was left before it
+        assert all(a >= c for a, c in zip(tail_lens, tail_lens[1:-1]))
+        assert tail_lens[-1] <= -(-(seg_len - (n - 1) * S) // 2)

@@ -31,12 +31,12 @@ def test_plan_slots_are_aligned_disjoint_and_owned_by_the_greedy_rule(numels, wo
 
 
 @settings(max_examples=150, deadline=None)
-@given(sizes_st, st.integers(min_value=2, max_value=9), rounds_st)
-def test_exchange_pieces_write_every_summed_element_once_per_round(numels, world, units):
+@given(sizes_st, st.integers(min_value=2, max_value=9), rounds_st, st.integers(min_value=0, max_value=5))
+def test_exchange_pieces_write_every_summed_element_once_per_round(numels, world, units, tail):
     p = layout.plan(numels, [HA_BF16] * len(numels), world)
     (cls,) = p.classes
     S = units * layout.ALIGN
-    pc = layout.exchange_pieces(cls, p.owner, numels, S)
+    pc = layout.exchange_pieces(cls, p.owner, numels, S, tail)
     written = {}
     covered = {i: np.zeros(numels[i], np.int8) for i in cls.indices}
     for t, so, o, do, c, r in zip(pc.tensor, pc.src_off, pc.owner, pc.dst_off, pc.count, pc.round):
@@ -45,7 +45,7 @@ def test_exchange_pieces_write_every_summed_element_once_per_round(numels, world
         w[do:do + c] += 1
         if t >= 0:
             i = cls.indices[t]
-            assert p.owner[i] == o and cls.offset[i] + so == r * S + do
+            assert p.owner[i] == o and cls.offset[i] + so == pc.bounds[r] + do
             covered[i][so:so + c] += 1
     assert all((v == 1).all() for v in covered.values())
     for o in range(world):
@@ -58,11 +58,11 @@ def test_exchange_pieces_write_every_summed_element_once_per_round(numels, world
 
 @settings(max_examples=100, deadline=None)
 @given(sizes_st, st.integers(min_value=2, max_value=9), rounds_st, st.integers(min_value=-1, max_value=4),
-       st.floats(min_value=0.0, max_value=1.0))
-def test_round_push_split_and_landing_pieces_partition(numels, world, units, streams, share):
+       st.floats(min_value=0.0, max_value=1.0), st.integers(min_value=0, max_value=3))
+def test_round_push_split_and_landing_pieces_partition(numels, world, units, streams, share, tail):
     p = layout.plan(numels, [HA_BF16] * len(numels), world)
     (cls,) = p.classes
-    pc = layout.exchange_pieces(cls, p.owner, numels, units * layout.ALIGN)
+    pc = layout.exchange_pieces(cls, p.owner, numels, units * layout.ALIGN, tail)
     for rank in range(world):
         for k in range(pc.n_rounds):
             kernel, groups = layout.round_push_split(pc, k, rank, streams, share, world)

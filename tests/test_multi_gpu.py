@@ -34,7 +34,8 @@ def _gpus() -> int:
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("mode", ["p2p", "p2p_rounds", "nccl", "p2p_landing", "p2p_rounds_landing",
                                   "p2p_landing_copyengine", "p2p_cepush", "p2p_rounds_cepush", "p2p_cegather",
-                                  "p2p_rounds_peerpush_cegather", "p2p_dirty", "p2p_rounds_cappedpush"])
+                                  "p2p_rounds_peerpush_cegather", "p2p_dirty", "p2p_rounds_cappedpush",
+                                  "p2p_rounds_tailsplit_landing"])
 @pytest.mark.parametrize("name", ["bf16_world2", "fp32_world2", "bf16_world2_inf"])
 def test_world2_matches_oracle_and_reference(name, mode, tmp_path):
     """*_landing*: gradients produced by two backward passes and pushed while they land
@@ -47,6 +48,8 @@ def test_world2_matches_oracle_and_reference(name, mode, tmp_path):
     # the landing modes) or by the push kernel (p2p, p2p_rounds)
     env["HYBRIDAGENT_B200_PUSH_STREAMS"] = ("peer" if "peerpush" in mode else
                                             "2" if ("cepush" in mode or "landing" in mode) else "0")
+    if "tailsplit" in mode:  # the last of the ~9 rounds cut into 3 more of halving length
+        env["HYBRIDAGENT_B200_TAIL_SPLIT"] = "3"
     if "cappedpush" in mode:  # the push kernel on a 3-CTA grid walking each round's chunk list
         env["HYBRIDAGENT_B200_PUSH_CTAS"] = "3"
     if mode == "p2p_dirty":  # rank 1 zeroes its copy of a tensor rank 0 owns before step 1

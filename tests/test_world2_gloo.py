@@ -164,7 +164,7 @@ def test_world2_host_path_matches_reference(name):
             assert_bits_equal(Z.narrow(master, Z.BF16), a, f"param[{i}]")
 
 
-def _rank_main_p2p(rank, world, port, name, queue):
+def _rank_main_p2p(rank, world, port, name, queue, tail=0):
     """The p2p data flow: in rounds (layout.exchange_pieces, a small round size so slots
     straddle rounds), each rank pushes each piece of its gradients to the address the
     product computes (half round % 2 of the owner's receive window, region <rank>), the
@@ -198,7 +198,7 @@ def _rank_main_p2p(rank, world, port, name, queue):
         S = 64 * max(2, 40 // world)  # small rounds: slots straddle rounds, both window halves are used
         recv_bases = [(r + 1) * SPACE for r in range(world)]               # each rank's receive window
         param_bases = [(r + 1) * SPACE + SPACE // 2 for r in range(world)]  # each rank's packed params
-        pieces = layout.exchange_pieces(cls, plan.owner, numels, S)
+        pieces = layout.exchange_pieces(cls, plan.owner, numels, S, tail)
         assert pieces.n_rounds > 4
         deltas = layout.peer_deltas(param_bases, rank)
         peers = [r for r in range(world) if r != rank]
@@ -248,7 +248,8 @@ def _rank_main_p2p(rank, world, port, name, queue):
                 acc = Z.widen(window[half:half + count].copy(), case.dtype)
                 for r in range(1, world):
                     acc = acc + Z.widen(window[half + r * S:half + r * S + count], case.dtype)
-                own[k * S:k * S + count] = Z.narrow(acc, case.dtype) if case.dtype != Z.F32 else acc
+                b = int(pieces.bounds[k])
+                own[b:b + count] = Z.narrow(acc, case.dtype) if case.dtype != Z.F32 else acc
             mine = {i: own[cls.offset[i]:cls.offset[i] + numels[i]].copy() for i in owned if used[i]}
             # like the product's fused sums: the whole reduced region, gaps included (all zero)
             total = torch.tensor([Z.sumsq(own[:cls.own_len[rank]].copy(), case.dtype)], dtype=torch.float64)
@@ -282,8 +283,8 @@ def _rank_main_p2p(rank, world, port, name, queue):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("name", ["bf16_world2"])
-def test_world2_p2p_host_path_matches_reference(name):
+@pytest.mark.parametrize("name,tail", [("bf16_world2", 0), ("bf16_world2", 2)])
+def test_world2_p2p_host_path_matches_reference(name, tail):
     import torch.multiprocessing as mp
 
     from helpers import Z, assert_bits_equal, assert_state_close, golden
@@ -292,7 +293,7 @@ def test_world2_p2p_host_path_matches_reference(name):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main_p2p, args=(r, 2, port, name, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main_p2p, args=(r, 2, port, name, q, tail)) for r in range(2)]
     for p in procs:
         p.start()
     results = {}
@@ -318,8 +319,8 @@ def test_world2_p2p_host_path_matches_reference(name):
         assert_bits_equal(Z.narrow(master, Z.BF16), a, f"param[{i}]")
 
 
-@pytest.mark.parametrize("world", [3, 4])
-def test_p2p_host_path_beyond_two_ranks_matches_oracle(world):
+@pytest.mark.parametrize("world,tail", [(3, 0), (4, 0), (3, 3)])
+def test_p2p_host_path_beyond_two_ranks_matches_oracle(world, tail):
     """The p2p data flow at W = 3 and 4 (gloo ranks on CPU; the GPU tests run W = 2 only):
     the product's piece layout, window addresses, rounds and peer offsets with the owner
     summing every rank's region in fp32 and rounding once, against the oracle's W-rank run
@@ -333,7 +334,7 @@ def test_p2p_host_path_beyond_two_ranks_matches_oracle(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main_p2p, args=(r, world, port, name, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main_p2p, args=(r, world, port, name, q, tail)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
