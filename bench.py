@@ -701,7 +701,7 @@ def run_ours(args) -> None:
         from types import SimpleNamespace
         barrier()
         info = SimpleNamespace(comm_mode=opt.comm_mode, push_streams=opt.push_streams, push_ctas=opt.push_ctas,
-                               gather_mode=opt.gather_mode)
+                               gather_mode=opt.gather_mode, tail_split=opt.tail_split)
         opt.close()
         opt = info
         params = inputs = None
@@ -803,6 +803,7 @@ def run_ours(args) -> None:
                    "parallelism": f"zero1_dp{world}",
                    "push": push_how if world > 1 and nvlink else None,
                    "all_gather": gather_how if world > 1 and nvlink else None,
+                   "tail_split": opt.tail_split if world > 1 and nvlink else None,
                    "l2": f"inputs larger than L2: {(n_params * 16) / 1e9 / world:.1f} GB of grads+state per GPU "
                          "per step vs 126 MB L2, no flush"},
         "roofline": roofline,
